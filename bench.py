@@ -1,0 +1,482 @@
+#!/usr/bin/env python
+"""Paged decode attention throughput on B200 (one decode step per iteration).
+
+Default workload: config 3 -- batch 256, GQA 32/8, head_dim 128, FP16 pages
+of 16 tokens, context lengths LogNormal(ln 8192, sigma=0.5) clipped to
+[512, 32768], sharded by sequence across the N GPUs (greedy length
+balancing), every GPU with its own TensorPagedKVCache and device pool, no
+collective.  A step is the SDK's decode transaction for the whole shard:
+pkv_step_begin (decode locks, reserve one token per sequence, page-table
+patch upload), pkv_kv_append of the new K/V rows, pkv_paged_decode, and
+pkv_step_end (commit lengths, release locks).
+
+  value  tokens/s of the whole job with Q and new K/V rows already in HBM
+         (total tokens of all ranks / max over ranks of the device step time)
+  e2e    the same step with Q and new K/V copied from pinned host memory and
+         the attention output copied back every step
+  roofline  the decode kernel: algorithmic bytes per launch (K+V of every
+         visible token, Q, O, block table) / mean launch time (CUDA events)
+  cpu_baseline  the SDK's own CPU attention (tensor_sdpa_f32 built from its
+         sources, oracle/_ref) on a sample of the same sequences, all host
+         threads; rank 0 at N=1 only
+
+--impl reference times only that SDK CPU path (rank 0; other ranks exit).
+Run under torchrun for N > 1 (RANK/LOCAL_RANK/WORLD_SIZE from the env).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from inference_c_b200 import workloads as W  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, choices=[2, 3], default=3)
+    p.add_argument("--chunk", type=int, default=0, help="decode split size in tokens (0: auto)")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="wall-time budget of the cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peak_hbm() -> tuple[float, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def metric_name(cfg: int) -> str:
+    return ("paged decode attention tokens/s (config %d: append 1 token per sequence + paged "
+            "SDPA per step)" % cfg)
+
+
+def config_block(cfg: int, n: int, chunk: int) -> dict:
+    c = W.CONFIGS[cfg]
+    d = {"workload": c.name, "batch": c.batch, "q_heads": c.q_heads, "kv_heads": c.kv_heads,
+         "head_dim": c.head_dim, "block_size": c.block_size, "storage": "f16",
+         "accumulate": "f32", "decode_chunk_tokens": chunk,
+         "parallelism": f"sequence-sharded over {n} GPU(s), one page pool per GPU, no collective",
+         "l2": "no flush needed: every step reads all visible pages (> 126 MB L2)"}
+    if cfg == 3:
+        d["lognormal_sigma"] = W.CFG3_SIGMA
+        d["lengths"] = "LogNormal(ln 8192, 0.5) clipped [512, 32768]"
+    else:
+        d["lengths"] = "U[1024, 4096]"
+    return d
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, uuid: str):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            u = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(u)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h) & ~0x1
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self) -> dict:
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": [n for b, n in self.REASONS.items() if self.reasons & b]}
+
+
+def auto_chunk(lengths: np.ndarray, kv_heads: int, sms: int = 148) -> int:
+    """Split size giving ~24 units per persistent CTA (2 CTAs per SM)."""
+    units = float(lengths.sum()) * kv_heads / (sms * 2 * 24)
+    c = int(math.ceil(max(units, 128) / 64.0) * 64)
+    return min(c, 4096)
+
+
+# ---------------------------------------------------------------------------
+# SDK CPU path (oracle/_ref): the reference arm and cpu_baseline
+# ---------------------------------------------------------------------------
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def host_sample_job(cfg: int, lengths: np.ndarray, picks: np.ndarray, seed: int):
+    """RefJob over host-generated FP16 pages for the chosen sequences."""
+    from oracle import oracle as O
+    c = W.CONFIGS[cfg]
+    rng = np.random.default_rng(seed + 99)
+    L = lengths[picks]
+    pages = (L + 15) // 16
+    rows = int(pages.sum()) * 16
+    k = rng.standard_normal((rows, c.kv_width), dtype=np.float32).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((rows, c.kv_width), dtype=np.float32).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal((len(picks), c.q_heads, c.head_dim), dtype=np.float32).astype(
+        np.float16).view(np.uint16)
+    tables = np.zeros((len(picks), int(pages.max())), np.uint32)
+    at = 0
+    for i, n in enumerate(pages):
+        tables[i, :n] = np.arange(at, at + n)
+        at += n
+    return O.RefJob("f16", q, None, k, v, c.kv_heads, c.head_dim, 16, tables, L, c.q_heads,
+                    c.scale, False)
+
+
+def stratified(lengths: np.ndarray, n: int) -> np.ndarray:
+    order = np.argsort(lengths, kind="stable")
+    idx = np.linspace(0, len(order) - 1, num=max(1, min(n, len(order)))).round().astype(int)
+    return np.unique(order[idx])
+
+
+def calibrate_sample(cfg: int, lengths: np.ndarray, threads: int, budget_s: float, seed: int):
+    """Sequences per sample so that one run of the SDK path takes ~budget_s."""
+    probe = stratified(lengths, threads)
+    job = host_sample_job(cfg, lengths, probe, seed)
+    t = job.run(threads)
+    job.close()
+    per_round = max(t, 1e-3)  # one sequence per thread, in parallel
+    rounds = max(1, int(budget_s / per_round))
+    picks = stratified(lengths, min(len(lengths), rounds * threads))
+    # bound host memory: at most ~300k context tokens (~2.5 GB widened to FP32)
+    while len(picks) > 1 and int(lengths[picks].sum()) > 300_000:
+        picks = stratified(lengths, len(picks) // 2)
+    return picks
+
+
+def sdk_cpu_rate(cfg: int, lengths: np.ndarray, budget_s: float, seed: int,
+                 repeats: int = 1) -> tuple[list[float], dict]:
+    threads = cpu_threads()
+    picks = calibrate_sample(cfg, lengths, threads, budget_s, seed)
+    job = host_sample_job(cfg, lengths, picks, seed)
+    times = [job.run(threads) for _ in range(repeats)]
+    job.close()
+    rates = [len(picks) / t for t in times]
+    info = {"cores": threads, "kind": "reference",
+            "sample": (f"{len(picks)} of {len(lengths)} sequences (stratified by length, "
+                       f"{int(lengths[picks].sum())} tokens of context) through the SDK's "
+                       f"tensor_sdpa_f32 built from its sources; gather+widen untimed")}
+    return rates, info
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lengths = W.context_lengths(args.config, args.seed)
+    threads = cpu_threads()
+    steps, warmup = args.steps, args.warmup
+    budget = max(0.05, 150.0 / max(1, steps + warmup))  # whole run within a few minutes
+    picks = calibrate_sample(args.config, lengths, threads, budget, args.seed)
+    job = host_sample_job(args.config, lengths, picks, args.seed)
+    for _ in range(warmup):
+        job.run(threads)
+    times = [job.run(threads) for _ in range(steps)]
+    job.close()
+    t = statistics.mean(times)
+    value = len(picks) / t
+    line = {
+        "metric": metric_name(args.config), "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "strong" if args.config == 3 else "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) FP16)",
+        "impl": "reference",
+        "config": config_block(args.config, args.gpus, 0),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": (f"each step: {len(picks)} of {len(lengths)} sequences "
+                                    "(stratified by length) through the SDK's tensor_sdpa_f32 "
+                                    "on all host threads; gather+widen untimed")},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args) -> None:
+    import torch
+
+    import inference_c_b200 as P
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    P.load()
+    cfg = args.config
+    c = W.CONFIGS[cfg]
+    if cfg == 3:
+        all_len = W.context_lengths(3, args.seed)
+        shard = W.shard_by_length(all_len, world)[rank]
+        lengths = all_len[shard]
+        total_seqs = len(all_len)
+    else:  # config 2 is a per-GPU batch of 32: weak scaling, one seed per rank
+        lengths = W.context_lengths(2, args.seed + rank)
+        total_seqs = len(lengths) * world
+    n = len(lengths)
+    steps, warmup = args.steps, args.warmup
+    e2e_steps = 0 if args.no_e2e else steps
+    grow = 2 * warmup + steps + e2e_steps + 2
+    chunk = args.chunk or auto_chunk(lengths + grow // 2, c.kv_heads)
+
+    # ---- cache, pool, fragmented tables, context import ----
+    pages_final = (lengths + grow + 15) // 16
+    pool_pages = int(math.ceil(pages_final.sum() * 1.1)) + 16
+    max_pages = int(pages_final.max()) + 1
+    cache = P.PagedKVCache(16, pool_pages, n)
+    pool = P.PagedPool(cache, local, P.PKV_DTYPE_F16, 1, c.kv_heads, c.head_dim, n, max_pages)
+    seqs = [cache.sequence_create() for _ in range(n)]
+    pages_now = (lengths + 15) // 16
+    picks = np.repeat(np.arange(n), pages_now)
+    picks = picks[W.permutation(args.seed + 7, len(picks), stream=rank)]
+    have = np.zeros(n, np.int64)
+    for b in picks:  # one page at a time, sequences in seeded random order
+        have[b] += 1
+        assert cache.reserve(seqs[b], int(min(lengths[b], 16 * have[b])))
+    pool.step_begin(seqs, lengths.tolist(), past_lengths=lengths.tolist())
+    batch = pool.step_batch()
+    layer = pool.layer(0)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
+    off_all = np.concatenate([[0], np.cumsum(lengths)])
+    start = 0
+    while start < n:  # import ~128 MB of rows at a time
+        stop = start
+        while stop < n and (off_all[stop + 1] - off_all[start]) * c.kv_width <= (64 << 20):
+            stop += 1
+        stop = max(stop, start + 1)
+        counts = np.zeros(n, np.int64)
+        counts[start:stop] = lengths[start:stop]
+        offs = torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).to(dev)
+        rows = int(counts.sum())
+        kr = torch.randn(rows, c.kv_width, generator=gen, device=dev).half()
+        vr = torch.randn(rows, c.kv_width, generator=gen, device=dev).half()
+        P.kv_import(layer, batch, kr, vr, offs)
+        del kr, vr
+        start = stop
+    pool.step_end(True)
+    torch.cuda.synchronize()
+
+    q = torch.randn(n, c.q_heads, c.head_dim, generator=gen, device=dev).half()
+    newk = torch.randn(n, c.kv_width, generator=gen, device=dev).half()
+    newv = torch.randn(n, c.kv_width, generator=gen, device=dev).half()
+    out = torch.empty(n, c.q_heads, c.head_dim, dtype=torch.float16, device=dev)
+    max_len = int(lengths.max()) + grow
+    ws = P.decode_workspace(n, c.q_heads, c.head_dim, max_len, chunk, device=dev)
+    stream = torch.cuda.current_stream()
+    ones = [1] * n
+    cur = lengths.copy()
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    launches = {"n": 0}
+    bytes_log: list[float] = []
+    kv_bytes_per_token = c.kv_width * 2 * 2
+
+    def step(i: int | None, q_in=None):
+        nonlocal cur
+        crossing = bool(((cur % 16) == 0).any())
+        pool.step_begin(seqs, ones)
+        b = pool.step_batch()
+        P.kv_append(layer, b, newk, newv)
+        if i is not None:
+            ev_a[i].record(stream)
+        P.paged_decode(layer, b, q if q_in is None else q_in, out, c.scale, max_len, ws, chunk)
+        if i is not None:
+            ev_b[i].record(stream)
+        pool.step_end(True)
+        cur = cur + 1
+        if i is not None:
+            launches["n"] += 2 + int(crossing)
+            bytes_log.append(float(cur.sum()) * kv_bytes_per_token + 2 * q.numel() * 2 +
+                             float(((cur + 15) // 16).sum()) * 4)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    with sampler:
+        for _ in range(warmup):
+            step(None)
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            step(i)
+        t1.record(stream)
+        barrier()
+        ms_step = t0.elapsed_time(t1) / steps
+        dec_ms = [a.elapsed_time(b) for a, b in zip(ev_a, ev_b)]
+        # ---- e2e: host buffers in, output back, every step ----
+        e2e = None
+        if e2e_steps:
+            h_q = torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
+            h_k = torch.empty(newk.shape, dtype=newk.dtype, pin_memory=True).copy_(newk.cpu())
+            h_v = torch.empty(newv.shape, dtype=newv.dtype, pin_memory=True).copy_(newv.cpu())
+            h_o = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            dq = torch.empty_like(q)
+
+            def e2e_step():
+                dq.copy_(h_q, non_blocking=True)
+                newk.copy_(h_k, non_blocking=True)
+                newv.copy_(h_v, non_blocking=True)
+                step(None, dq)
+                h_o.copy_(out, non_blocking=True)
+                stream.synchronize()
+
+            for _ in range(warmup):
+                e2e_step()
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(e2e_steps):
+                e2e_step()
+            e1.record(stream)
+            barrier()
+            e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+            h2d = (h_q.numel() + h_k.numel() + h_v.numel()) * 2
+            d2h = h_o.numel() * 2
+            e2e = {"value": total_seqs / (e2e_ms / 1e3), "unit": "tokens/s",
+                   "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
+                   "d2h_bytes_per_step": d2h * world,
+                   "api": "pkv_step_begin/pkv_kv_append/pkv_paged_decode/pkv_step_end + "
+                          "pinned host<->device copies"}
+    fault = P.device_fault(local)
+    if fault:
+        raise SystemExit(f"device fault code {fault} recorded during the bench")
+    ms_max = max_over_ranks(ms_step)
+    mean_dec = statistics.mean(dec_ms)
+    alg_bytes = statistics.mean(bytes_log)
+    peak, peak_kind = peak_hbm()
+    achieved = alg_bytes / (mean_dec / 1e3) / 1e9
+    per_rank = {"rank": rank, "decode_ms": mean_dec, "gbs": achieved, "seqs": n,
+                "tokens": int(cur.sum())}
+    gathered = [per_rank]
+    if dist is not None:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, per_rank)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            rates, info = sdk_cpu_rate(cfg, lengths, args.cpu_seconds, args.seed)
+            cpu = {"value": rates[0], "unit": "tokens/s", **info}
+        except FileNotFoundError as e:
+            cpu = {"value": None, "unit": "tokens/s", "cores": cpu_threads(), "kind": "reference",
+                   "sample": f"unavailable: {e}"}
+    if rank == 0:
+        line = {
+            "metric": metric_name(cfg),
+            "value": total_seqs / (ms_max / 1e3),
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms_max,
+            "higher_is_better": True,
+            "scaling": "strong" if cfg == 3 else "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic: seeded N(0,1) FP16 Q/K/V on the device, seeded lengths",
+            "config": config_block(cfg, world, chunk),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_kind": peak_kind, "kernel": "paged_decode_kernel",
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "mean_launch_ms": mean_dec, "per_rank": gathered},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches["n"],
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    cache.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+/*
+ * pkv_b200.h -- B200 (sm_100a) paged-KV attention: the C ABI.
+ *
+ * Two layers, both plain C (no C++ or torch types cross this boundary):
+ *
+ *  1. Kernel entry points.  Device pointers in, device pointers out, one CUDA
+ *     stream per call.  Each replaces one piece of the inference SDK's CUDA
+ *     backend (src/platform/cuda/attention_cuda.cu) and batches it over many
+ *     sequences per launch instead of one sequence per call.
+ *
+ *  2. Host transaction layer (C11).  A device page pool attached to a
+ *     TensorPagedKVCache through tensor_paged_kv_cache_set_backend_state
+ *     (the SDK's own attach point), plus a batch version of the transaction
+ *     in tensor_attention_decode_sequence_paged (src/common/attention.c:124-176):
+ *     begin_decode -> length check -> reserve -> kernels -> set_length or
+ *     rollback -> end_decode, for every sequence of a batch at once.
+ *
+ * Conventions (same as the SDK): every int-returning call gives 1 on success
+ * and 0 on failure; calls that take (error, error_capacity) write a
+ * NUL-terminated reason there on failure (either may be NULL/0).
+ *
+ * Pool layout (SDK attention_cuda.cu:301-305 and :547-612): one K pool and
+ * one V pool per layer, each [block_count * block_size][kv_heads * head_dim]
+ * elements of 2 bytes.  Token `pos` of a sequence lives in row
+ *     table[pos / block_size] * block_size + pos % block_size
+ * and KV head h occupies columns [h * head_dim, (h + 1) * head_dim).
+ *
+ * Block tables are dense and padded: row b (the b-th sequence of a batch)
+ * starts at block_tables + b * table_stride and lists that sequence's page ids
+ * in logical order.  seq_lens[b] is the sequence length AFTER this step's
+ * append: append writes the last n_b positions, attention reads all of them.
+ */
+#ifndef PKV_B200_H
+#define PKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "paged_kv_cache.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL selects the legacy default stream. */
+typedef struct CUstream_st *PkvStream;
+
+typedef enum {
+    PKV_DTYPE_F16 = 1,
+    PKV_DTYPE_BF16 = 2,
+    PKV_DTYPE_F32 = 3 /* outputs only */
+} PkvDType;
+
+/* One layer of a device page pool. */
+typedef struct {
+    void *key_pool;
+    void *value_pool;
+    size_t block_size;  /* tokens per page */
+    size_t block_count; /* pages in the pool (device bounds checks use it) */
+    size_t kv_heads;
+    size_t head_dim;    /* 64 or 128 */
+    PkvDType dtype;     /* storage: F16 or BF16 */
+} PkvPagedLayer;
+
+/* The sequences of one batch, as the kernels see them (device pointers). */
+typedef struct {
+    const uint32_t *block_tables; /* [batch][table_stride] page ids */
+    size_t table_stride;          /* >= pages of the longest sequence */
+    const int32_t *seq_lens;      /* [batch] lengths after this step's append */
+    size_t batch;
+} PkvBatch;
+
+/* ---------------------------------------------------------------------- */
+/* 1. Kernel entry points                                                  */
+/* ---------------------------------------------------------------------- */
+
+/* KV append: scatters new K/V rows into their pages with 16-byte stores.
+ * Rows row_offsets[b] .. row_offsets[b+1]-1 of key_rows/value_rows
+ * ([total_rows][kv_heads*head_dim], pool dtype) become positions
+ * seq_lens[b]-n_b .. seq_lens[b]-1 of sequence b.  row_offsets == NULL means
+ * one row per sequence (row b belongs to sequence b, total_rows == batch).
+ * Replaces the K/V stores of decode_rope_cache_kernel
+ * (attention_cuda.cu:307-341, launched :996-1000), without RoPE. */
+int pkv_kv_append(const PkvPagedLayer *layer, const PkvBatch *batch,
+                  const int32_t *row_offsets, const void *key_rows,
+                  const void *value_rows, size_t total_rows, PkvStream stream,
+                  char *error, size_t error_capacity);
+
+/* Prefix import: copies each sequence's contiguous K/V prefix
+ * ([sum seq_lens][kv_width], sequences back to back in batch order) into its
+ * pages, all sequences in one launch.  Replaces the per-page-run cudaMemcpy
+ * loop of attention_cuda.cu:894-915. */
+int pkv_kv_import(const PkvPagedLayer *layer, const PkvBatch *batch,
+                  const int32_t *row_offsets, const void *key_rows,
+                  const void *value_rows, size_t total_rows, PkvStream stream,
+                  char *error, size_t error_capacity);
+
+/* Gather: the inverse of import.  Writes sequence b's first seq_lens[b]
+ * tokens to rows row_offsets[b] .. of key_out/value_out.  The SDK never reads
+ * pages back (attention_cuda.cu:1084-1086); this exists for checkpointing and
+ * for the bit-exact page tests. */
+int pkv_kv_gather(const PkvPagedLayer *layer, const PkvBatch *batch,
+                  const int32_t *row_offsets, void *key_out, void *value_out,
+                  size_t total_rows, PkvStream stream, char *error,
+                  size_t error_capacity);
+
+/* Scratch needed by pkv_paged_decode for this shape (bytes). */
+size_t pkv_decode_workspace_bytes(size_t batch, size_t q_heads,
+                                  size_t head_dim, size_t max_seq_len,
+                                  size_t chunk_tokens);
+/* Decode scratch must start zeroed once; pkv_paged_decode leaves it zeroed. */
+int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes,
+                              PkvStream stream, char *error,
+                              size_t error_capacity);
+
+/* Paged decode SDPA, one query token per sequence, GQA.
+ * query/output: [batch][q_heads][head_dim]; output dtype F16, BF16 or F32.
+ * Each CTA owns one (sequence, KV head, chunk of chunk_tokens positions):
+ * the KV head's pages are staged once in shared memory for all
+ * q_heads/kv_heads query heads, scores use an online (running-max) softmax in
+ * FP32 and chunks of one sequence are merged by the last CTA to finish.
+ * max_seq_len bounds seq_lens (it sizes the scratch); chunk_tokens 0 picks a
+ * split from batch and max_seq_len.  seq_lens[b] == 0 yields zeros, like the
+ * SDK's all-masked softmax.  Replaces decode_score_kernel,
+ * decode_softmax_kernel and decode_attention_output_kernel
+ * (attention_cuda.cu:343-398, launched :1001-1011). */
+int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch,
+                     size_t q_heads, const void *query, float scale,
+                     void *output, PkvDType output_dtype, size_t max_seq_len,
+                     size_t chunk_tokens, void *workspace,
+                     size_t workspace_bytes, PkvStream stream, char *error,
+                     size_t error_capacity);
+
+/* Chunked prefill over the paged cache (tcgen05 tensor cores, FP32
+ * accumulation in TMEM).  Sequence b contributes query rows
+ * query_offsets[b] .. query_offsets[b+1]-1 ([total_q][q_heads][head_dim]);
+ * they are its LAST n_b positions, so query j sees keys
+ * 0 .. seq_lens[b]-n_b+j when causal (the SDK's causal offset
+ * kv_len - q_len, attention.c:251,352) and all seq_lens[b] keys otherwise.
+ * max_query_len bounds n_b.  Replaces the dense sdpa<T> path
+ * (attention_cuda.cu:25-99 via tensor_sdpa_f16, attention.c:408-459). */
+int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch,
+                      size_t q_heads, const int32_t *query_offsets,
+                      const void *query, size_t total_query_rows,
+                      size_t max_query_len, float scale, int causal,
+                      void *output, PkvDType output_dtype, PkvStream stream,
+                      char *error, size_t error_capacity);
+
+/* Reads and clears the device fault word of `device` (synchronises it).
+ * Kernels never trap: an out-of-range page id or position skips the access
+ * and records a code here.  *code == 0 means no fault was recorded. */
+int pkv_device_fault(int device, uint32_t *code, char *error,
+                     size_t error_capacity);
+
+/* ---------------------------------------------------------------------- */
+/* 2. Host transaction layer                                               */
+/* ---------------------------------------------------------------------- */
+
+typedef struct PkvPool PkvPool;
+
+/* Allocates layer_count K and V pools on `device` for every page of `cache`,
+ * a padded device block table for up to max_batch sequences of up to
+ * max_pages_per_seq pages, and attaches the pool to the cache as its CUDA
+ * backend state (tensor_paged_kv_cache_free destroys it).  Pools start
+ * zeroed.  Replaces get_cuda_paged_kv_state (attention_cuda.cu:570-612). */
+int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
+                    size_t layer_count, size_t kv_heads, size_t head_dim,
+                    size_t max_batch, size_t max_pages_per_seq,
+                    PkvPool **pool, char *error, size_t error_capacity);
+/* The pool attached to `cache`, or NULL. */
+PkvPool *pkv_pool_from_cache(TensorPagedKVCache *cache);
+/* Device view of one layer. */
+int pkv_pool_layer(PkvPool *pool, size_t layer, PkvPagedLayer *out);
+
+/* Opens a batch step: for each sequence (in order; row b of the batch) takes
+ * the decode lock, checks its length is 0 or past_lengths[b] (NULL: accept
+ * the current length), reserves past + new_tokens[b] tokens, and stages the
+ * new page-table entries and lengths for the device on `stream`.  All or
+ * nothing: any failure rolls every sequence back and releases its lock. */
+int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
+                   const size_t *past_lengths, const size_t *new_tokens,
+                   size_t batch, PkvStream stream, char *error,
+                   size_t error_capacity);
+/* Device view of the open step (block tables, post-append lengths). */
+int pkv_step_batch(PkvPool *pool, PkvBatch *out);
+/* Device row offsets of the open step's new tokens ([batch+1], int32). */
+const int32_t *pkv_step_row_offsets(PkvPool *pool);
+/* Closes the step: commit sets every length to past + new; otherwise the
+ * reservations are rolled back.  Always releases the decode locks. */
+int pkv_step_end(PkvPool *pool, int commit, char *error,
+                 size_t error_capacity);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

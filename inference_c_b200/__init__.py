@@ -1,0 +1,346 @@
+"""B200 (sm_100a) paged-KV attention behind the inference SDK's C API.
+
+The product is the shared library ``inference_c_b200/lib/libpkv_b200.so``:
+C11 host code (page allocator with the SDK's ``tensor_paged_kv_*`` API, the
+device pool and the batch step transaction) and the CUDA kernels, exported
+through ``include/paged_kv_cache.h`` and ``include/pkv_b200.h``.  This module
+is the Python view of that ABI, via ctypes: tests and ``bench.py`` use it,
+with torch only for device memory and streams.  Nothing here computes
+attention; there is no CPU fallback, and every call raises when the library
+is missing or a C call reports failure.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+from typing import Optional, Sequence
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "lib" / "libpkv_b200.so"
+
+PKV_DTYPE_F16 = 1
+PKV_DTYPE_BF16 = 2
+PKV_DTYPE_F32 = 3
+
+TENSOR_PAGED_KV_BACKEND_CUDA = 1
+
+_c_size = ctypes.c_size_t
+_c_ptr = ctypes.c_void_p
+_c_u64 = ctypes.c_uint64
+_c_int = ctypes.c_int
+_c_char_p = ctypes.c_char_p
+
+
+class PkvPagedLayer(ctypes.Structure):
+    _fields_ = [
+        ("key_pool", _c_ptr),
+        ("value_pool", _c_ptr),
+        ("block_size", _c_size),
+        ("block_count", _c_size),
+        ("kv_heads", _c_size),
+        ("head_dim", _c_size),
+        ("dtype", _c_int),
+    ]
+
+
+class PkvBatch(ctypes.Structure):
+    _fields_ = [
+        ("block_tables", _c_ptr),
+        ("table_stride", _c_size),
+        ("seq_lens", _c_ptr),
+        ("batch", _c_size),
+    ]
+
+
+_LP = ctypes.POINTER(PkvPagedLayer)
+_BP = ctypes.POINTER(PkvBatch)
+_ERR = [_c_char_p, _c_size]
+
+# name -> (restype, argtypes).  Every symbol declared in include/*.h.
+EXPORTS = {
+    # include/paged_kv_cache.h
+    "tensor_paged_kv_cache_create": (_c_int, [_c_size, _c_size, _c_size, ctypes.POINTER(_c_ptr)]),
+    "tensor_paged_kv_cache_free": (None, [_c_ptr]),
+    "tensor_paged_kv_sequence_create": (_c_int, [_c_ptr, ctypes.POINTER(_c_u64)]),
+    "tensor_paged_kv_sequence_reserve": (_c_int, [_c_ptr, _c_u64, _c_size]),
+    "tensor_paged_kv_sequence_set_length": (_c_int, [_c_ptr, _c_u64, _c_size]),
+    "tensor_paged_kv_sequence_copy_block_table": (
+        _c_int, [_c_ptr, _c_u64, _c_ptr, _c_size, ctypes.POINTER(_c_size)]),
+    "tensor_paged_kv_sequence_length": (_c_int, [_c_ptr, _c_u64, ctypes.POINTER(_c_size)]),
+    "tensor_paged_kv_sequence_release": (_c_int, [_c_ptr, _c_u64]),
+    "tensor_paged_kv_sequence_begin_decode": (_c_int, [_c_ptr, _c_u64]),
+    "tensor_paged_kv_sequence_end_decode": (None, [_c_ptr, _c_u64]),
+    "tensor_paged_kv_cache_free_blocks": (_c_size, [_c_ptr]),
+    "tensor_paged_kv_cache_block_size": (_c_size, [_c_ptr]),
+    "tensor_paged_kv_cache_block_count": (_c_size, [_c_ptr]),
+    "tensor_paged_kv_cache_backend_state": (_c_ptr, [_c_ptr, _c_int]),
+    "tensor_paged_kv_cache_set_backend_state": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr]),
+    # include/pkv_b200.h -- kernels
+    "pkv_kv_append": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_kv_import": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_kv_gather": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_decode_workspace_bytes": (_c_size, [_c_size, _c_size, _c_size, _c_size, _c_size]),
+    "pkv_decode_workspace_init": (_c_int, [_c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_paged_decode": (_c_int, [_LP, _BP, _c_size, _c_ptr, ctypes.c_float, _c_ptr, _c_int,
+                                  _c_size, _c_size, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_paged_prefill": (_c_int, [_LP, _BP, _c_size, _c_ptr, _c_ptr, _c_size, _c_size,
+                                   ctypes.c_float, _c_int, _c_ptr, _c_int, _c_ptr, *_ERR]),
+    "pkv_device_fault": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_uint32), *_ERR]),
+    # include/pkv_b200.h -- host transaction layer
+    "pkv_pool_create": (_c_int, [_c_ptr, _c_int, _c_int, _c_size, _c_size, _c_size, _c_size,
+                                 _c_size, ctypes.POINTER(_c_ptr), *_ERR]),
+    "pkv_pool_from_cache": (_c_ptr, [_c_ptr]),
+    "pkv_pool_layer": (_c_int, [_c_ptr, _c_size, _LP]),
+    "pkv_step_begin": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_step_batch": (_c_int, [_c_ptr, _BP]),
+    "pkv_step_row_offsets": (_c_ptr, [_c_ptr]),
+    "pkv_step_end": (_c_int, [_c_ptr, _c_int, *_ERR]),
+}
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libpkv_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: run inference_c_b200/_build.py "
+                           "(or __graft_entry__.build()) first; there is no fallback")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class PkvError(RuntimeError):
+    """A C entry point returned 0."""
+
+
+def _call(name: str, *args):
+    lib = load()
+    err = ctypes.create_string_buffer(512)
+    ok = getattr(lib, name)(*args, err, len(err))
+    if not ok:
+        raise PkvError(f"{name}: {err.value.decode(errors='replace')}")
+    return ok
+
+
+# ---------------------------------------------------------------------------
+# Allocator: the SDK's tensor_paged_kv_* API, one method per C function.
+# ---------------------------------------------------------------------------
+
+class PagedKVCache:
+    """Owns one TensorPagedKVCache*.  Methods return the C result (1/0)."""
+
+    def __init__(self, block_size: int, block_count: int, max_sequences: int):
+        lib = load()
+        h = _c_ptr()
+        if not lib.tensor_paged_kv_cache_create(block_size, block_count, max_sequences,
+                                                ctypes.byref(h)):
+            raise PkvError("tensor_paged_kv_cache_create failed")
+        self.handle = h.value
+        self._lib = lib
+
+    def free(self) -> None:
+        if self.handle:
+            self._lib.tensor_paged_kv_cache_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def sequence_create(self) -> int:
+        s = _c_u64(0)
+        return s.value if self._lib.tensor_paged_kv_sequence_create(self.handle, ctypes.byref(s)) else 0
+
+    def reserve(self, seq: int, tokens: int) -> int:
+        return self._lib.tensor_paged_kv_sequence_reserve(self.handle, seq, tokens)
+
+    def set_length(self, seq: int, tokens: int) -> int:
+        return self._lib.tensor_paged_kv_sequence_set_length(self.handle, seq, tokens)
+
+    def length(self, seq: int) -> Optional[int]:
+        n = _c_size(0)
+        return n.value if self._lib.tensor_paged_kv_sequence_length(self.handle, seq, ctypes.byref(n)) else None
+
+    def block_table(self, seq: int) -> Optional[list[int]]:
+        n = _c_size(0)
+        if not self._lib.tensor_paged_kv_sequence_copy_block_table(self.handle, seq, None, 0,
+                                                                   ctypes.byref(n)):
+            return None
+        buf = (ctypes.c_uint32 * max(1, n.value))()
+        if not self._lib.tensor_paged_kv_sequence_copy_block_table(self.handle, seq, buf, n.value,
+                                                                   ctypes.byref(n)):
+            return None
+        return list(buf[: n.value])
+
+    def copy_block_table(self, seq: int, capacity: int) -> tuple[int, list[int], int]:
+        buf = (ctypes.c_uint32 * max(1, capacity))()
+        n = _c_size(0)
+        ok = self._lib.tensor_paged_kv_sequence_copy_block_table(self.handle, seq, buf, capacity,
+                                                                 ctypes.byref(n))
+        return ok, list(buf[: min(n.value, capacity)]), n.value
+
+    def release(self, seq: int) -> int:
+        return self._lib.tensor_paged_kv_sequence_release(self.handle, seq)
+
+    def begin_decode(self, seq: int) -> int:
+        return self._lib.tensor_paged_kv_sequence_begin_decode(self.handle, seq)
+
+    def end_decode(self, seq: int) -> None:
+        self._lib.tensor_paged_kv_sequence_end_decode(self.handle, seq)
+
+    def free_blocks(self) -> int:
+        return self._lib.tensor_paged_kv_cache_free_blocks(self.handle)
+
+    def block_size(self) -> int:
+        return self._lib.tensor_paged_kv_cache_block_size(self.handle)
+
+    def block_count(self) -> int:
+        return self._lib.tensor_paged_kv_cache_block_count(self.handle)
+
+
+# ---------------------------------------------------------------------------
+# Kernel entry points over torch tensors (device memory only).
+# ---------------------------------------------------------------------------
+
+def _ptr(x) -> Optional[int]:
+    """Device address of a tensor, or an int address passed through."""
+    if x is None or isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _dtype_code(t) -> int:
+    import torch
+    return {torch.float16: PKV_DTYPE_F16, torch.bfloat16: PKV_DTYPE_BF16,
+            torch.float32: PKV_DTYPE_F32}[t.dtype]
+
+
+def _stream_ptr(stream) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def make_layer(key_pool, value_pool, block_size: int, kv_heads: int, head_dim: int) -> PkvPagedLayer:
+    """Layer view of two [block_count*block_size, kv_heads*head_dim] pools."""
+    assert key_pool.shape == value_pool.shape and key_pool.is_cuda
+    rows = key_pool.shape[0]
+    assert rows % block_size == 0 and key_pool.shape[1] == kv_heads * head_dim
+    return PkvPagedLayer(key_pool.data_ptr(), value_pool.data_ptr(), block_size,
+                         rows // block_size, kv_heads, head_dim, _dtype_code(key_pool))
+
+
+def make_batch(block_tables, seq_lens) -> PkvBatch:
+    """Batch view of a [batch, stride] int32 table and [batch] int32 lengths."""
+    assert block_tables.dim() == 2 and block_tables.is_contiguous() and seq_lens.is_contiguous()
+    return PkvBatch(block_tables.data_ptr(), block_tables.shape[1], seq_lens.data_ptr(),
+                    block_tables.shape[0])
+
+
+def kv_append(layer: PkvPagedLayer, batch: PkvBatch, key_rows, value_rows, row_offsets=None,
+              stream=None) -> None:
+    _call("pkv_kv_append", ctypes.byref(layer), ctypes.byref(batch), _ptr(row_offsets),
+          key_rows.data_ptr(), value_rows.data_ptr(), key_rows.shape[0], _stream_ptr(stream))
+
+
+def kv_import(layer: PkvPagedLayer, batch: PkvBatch, key_rows, value_rows, row_offsets,
+              stream=None) -> None:
+    _call("pkv_kv_import", ctypes.byref(layer), ctypes.byref(batch), _ptr(row_offsets),
+          key_rows.data_ptr(), value_rows.data_ptr(), key_rows.shape[0], _stream_ptr(stream))
+
+
+def kv_gather(layer: PkvPagedLayer, batch: PkvBatch, key_out, value_out, row_offsets,
+              stream=None) -> None:
+    _call("pkv_kv_gather", ctypes.byref(layer), ctypes.byref(batch), _ptr(row_offsets),
+          key_out.data_ptr(), value_out.data_ptr(), key_out.shape[0], _stream_ptr(stream))
+
+
+def decode_workspace_bytes(batch: int, q_heads: int, head_dim: int, max_seq_len: int,
+                           chunk_tokens: int = 0) -> int:
+    return load().pkv_decode_workspace_bytes(batch, q_heads, head_dim, max_seq_len, chunk_tokens)
+
+
+def decode_workspace(batch: int, q_heads: int, head_dim: int, max_seq_len: int,
+                     chunk_tokens: int = 0, device=None, stream=None):
+    """Zero-initialised decode scratch as a uint8 CUDA tensor."""
+    import torch
+    n = decode_workspace_bytes(batch, q_heads, head_dim, max_seq_len, chunk_tokens)
+    ws = torch.empty(n, dtype=torch.uint8, device=device or "cuda")
+    _call("pkv_decode_workspace_init", ws.data_ptr(), n, _stream_ptr(stream))
+    return ws
+
+
+def paged_decode(layer: PkvPagedLayer, batch: PkvBatch, query, output, scale: float,
+                 max_seq_len: int, workspace, chunk_tokens: int = 0, stream=None) -> None:
+    q_heads = query.shape[-2]
+    _call("pkv_paged_decode", ctypes.byref(layer), ctypes.byref(batch), q_heads,
+          query.data_ptr(), ctypes.c_float(scale), output.data_ptr(), _dtype_code(output),
+          max_seq_len, chunk_tokens, workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+
+
+def paged_prefill(layer: PkvPagedLayer, batch: PkvBatch, query, query_offsets, output,
+                  scale: float, max_query_len: int, causal: bool = True, stream=None) -> None:
+    q_heads = query.shape[-2]
+    _call("pkv_paged_prefill", ctypes.byref(layer), ctypes.byref(batch), q_heads,
+          _ptr(query_offsets), query.data_ptr(), query.shape[0], max_query_len,
+          ctypes.c_float(scale), int(causal), output.data_ptr(), _dtype_code(output),
+          _stream_ptr(stream))
+
+
+def device_fault(device: int = 0) -> int:
+    code = ctypes.c_uint32(0)
+    _call("pkv_device_fault", device, ctypes.byref(code))
+    return code.value
+
+
+# ---------------------------------------------------------------------------
+# Host transaction layer.
+# ---------------------------------------------------------------------------
+
+class PagedPool:
+    """Device pool attached to a PagedKVCache (freed with the cache)."""
+
+    def __init__(self, cache: PagedKVCache, device: int, dtype: int, layer_count: int,
+                 kv_heads: int, head_dim: int, max_batch: int, max_pages_per_seq: int):
+        h = _c_ptr()
+        _call("pkv_pool_create", cache.handle, device, dtype, layer_count, kv_heads, head_dim,
+              max_batch, max_pages_per_seq, ctypes.byref(h))
+        self.handle = h.value
+        self.cache = cache
+        self.max_batch = max_batch
+        self._lib = load()
+
+    def layer(self, index: int) -> PkvPagedLayer:
+        out = PkvPagedLayer()
+        if not self._lib.pkv_pool_layer(self.handle, index, ctypes.byref(out)):
+            raise PkvError(f"pkv_pool_layer({index}) failed")
+        return out
+
+    def step_begin(self, sequences: Sequence[int], new_tokens: Sequence[int],
+                   past_lengths: Optional[Sequence[int]] = None, stream=None) -> None:
+        n = len(sequences)
+        seqs = (_c_u64 * n)(*sequences)
+        new = (_c_size * n)(*new_tokens)
+        past = None if past_lengths is None else (_c_size * n)(*past_lengths)
+        _call("pkv_step_begin", self.handle, seqs, past, new, n, _stream_ptr(stream))
+
+    def step_batch(self) -> PkvBatch:
+        out = PkvBatch()
+        if not self._lib.pkv_step_batch(self.handle, ctypes.byref(out)):
+            raise PkvError("pkv_step_batch: no open step")
+        return out
+
+    def step_row_offsets(self) -> int:
+        return self._lib.pkv_step_row_offsets(self.handle)
+
+    def step_end(self, commit: bool) -> None:
+        _call("pkv_step_end", self.handle, int(commit))

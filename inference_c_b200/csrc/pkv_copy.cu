@@ -1,0 +1,233 @@
+// pkv_copy.cu -- KV append / prefix import / gather through the block table.
+//
+// All three are the same bandwidth-bound row copy between a contiguous
+// [rows][kv_width] buffer and the paged pool, one warp per token row, 16-byte
+// vector loads and stores (a 2 KiB Llama-3-8B row is 4 uint4 per lane for K
+// and 4 for V, all issued before the first store).  The page address of a
+// position follows the SDK's decode_kv_position (attention_cuda.cu:301-305).
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "pkv_device.cuh"
+#include "pkv_internal.h"
+
+namespace pkv {
+namespace {
+
+__device__ uint32_t g_copy_fault;
+
+constexpr int kCopyWarps = 8;
+
+// Sequence owning contiguous row `row`: largest b with offsets[b] <= row.
+__device__ __forceinline__ int find_sequence(const int32_t *offsets, int batch, int32_t row) {
+    int lo = 0, hi = batch - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(offsets + mid) <= row) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// TO_POOL: rows -> pages (append, import).  Otherwise pages -> rows (gather).
+// `tail` selects where a sequence's rows land: its last n_b positions
+// (append) or its first n_b positions (import, gather).
+template <bool TO_POOL, int VEC>
+__global__ void __launch_bounds__(kCopyWarps * 32)
+kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
+               uint4 *__restrict__ krows, uint4 *__restrict__ vrows,
+               const uint32_t *__restrict__ tables, int32_t table_stride,
+               const int32_t *__restrict__ seq_lens, const int32_t *__restrict__ offsets,
+               int batch, int32_t total_rows, int vec_per_row, int block_size,
+               int block_shift, uint32_t block_count, bool tail) {
+    const int lane = threadIdx.x & 31;
+    const int32_t row = blockIdx.x * kCopyWarps + (threadIdx.x >> 5);
+    if (row >= total_rows) return;
+    int b;
+    int32_t first, count;
+    if (offsets == nullptr) {
+        b = row;
+        first = row;
+        count = 1;
+    } else {
+        b = find_sequence(offsets, batch, row);
+        first = __ldg(offsets + b);
+        count = __ldg(offsets + b + 1) - first;
+    }
+    const int32_t len = __ldg(seq_lens + b);
+    if (count > len) {
+        if (lane == 0) record_fault(&g_copy_fault, kFaultRowsMismatch);
+        return;
+    }
+    const int32_t pos = (tail ? len - count : 0) + (row - first);
+    PageMap map{tables + (int64_t)b * table_stride, block_size, block_shift, block_count,
+                table_stride};
+    int64_t prow = 0;
+    const uint32_t fault = map.row_of(pos, prow);
+    if (fault != kFaultNone) {
+        if (lane == 0) record_fault(&g_copy_fault, fault);
+        return;
+    }
+    const int64_t src = (int64_t)row * vec_per_row;
+    const int64_t dst = prow * vec_per_row;
+    if constexpr (VEC > 0) {
+        // Fixed row width: load everything first, then store.
+        uint4 k[VEC], v[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            const int c = lane + 32 * i;
+            k[i] = TO_POOL ? __ldg(krows + src + c) : __ldg(kpool + dst + c);
+            v[i] = TO_POOL ? __ldg(vrows + src + c) : __ldg(vpool + dst + c);
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            const int c = lane + 32 * i;
+            if (TO_POOL) { kpool[dst + c] = k[i]; vpool[dst + c] = v[i]; }
+            else { krows[src + c] = k[i]; vrows[src + c] = v[i]; }
+        }
+    } else {
+        for (int c = lane; c < vec_per_row; c += 32) {
+            if (TO_POOL) {
+                kpool[dst + c] = __ldg(krows + src + c);
+                vpool[dst + c] = __ldg(vrows + src + c);
+            } else {
+                krows[src + c] = __ldg(kpool + dst + c);
+                vrows[src + c] = __ldg(vpool + dst + c);
+            }
+        }
+    }
+}
+
+__global__ void apply_patches_kernel(uint32_t *table, int64_t stride, int64_t rows,
+                                     const PkvTablePatch *patches, int64_t count) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const PkvTablePatch p = patches[i];
+    if ((int64_t)p.row >= rows || (int64_t)p.index >= stride) {
+        record_fault(&g_copy_fault, kFaultPositionOutOfRange);
+        return;
+    }
+    table[(int64_t)p.row * stride + p.index] = p.page;
+}
+
+int block_shift_of(size_t block_size) {
+    if (block_size == 0 || (block_size & (block_size - 1)) != 0) return -1;
+    int s = 0;
+    while ((size_t(1) << s) < block_size) ++s;
+    return s;
+}
+
+template <bool TO_POOL>
+int launch_rows(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *offsets,
+                const void *krows, const void *vrows, size_t total_rows, bool tail,
+                PkvStream stream, char *error, size_t cap, const char *what) {
+    if (layer == nullptr || batch == nullptr || layer->key_pool == nullptr ||
+        layer->value_pool == nullptr || krows == nullptr || vrows == nullptr ||
+        batch->block_tables == nullptr || batch->seq_lens == nullptr) {
+        pkv_internal_set_error(error, cap, "%s: null argument", what);
+        return 0;
+    }
+    if (layer->dtype != PKV_DTYPE_F16 && layer->dtype != PKV_DTYPE_BF16) {
+        pkv_internal_set_error(error, cap, "%s: pool dtype must be F16 or BF16", what);
+        return 0;
+    }
+    const size_t kv_width = layer->kv_heads * layer->head_dim;
+    if (kv_width == 0 || (kv_width * 2) % 16 != 0 || layer->block_size == 0 ||
+        layer->block_count == 0 || batch->batch == 0 || batch->table_stride == 0 ||
+        total_rows > INT32_MAX || batch->batch > INT32_MAX ||
+        batch->table_stride > INT32_MAX || layer->block_size > INT32_MAX ||
+        layer->block_count > UINT32_MAX) {
+        pkv_internal_set_error(error, cap,
+                               "%s: invalid shape (kv_width*2 must be a multiple of 16 bytes)",
+                               what);
+        return 0;
+    }
+    if (offsets == nullptr && total_rows != batch->batch) {
+        pkv_internal_set_error(error, cap, "%s: one row per sequence needs total_rows == batch",
+                               what);
+        return 0;
+    }
+    if (((uintptr_t)layer->key_pool | (uintptr_t)layer->value_pool | (uintptr_t)krows |
+         (uintptr_t)vrows) % 16 != 0) {
+        pkv_internal_set_error(error, cap, "%s: buffers must be 16-byte aligned", what);
+        return 0;
+    }
+    if (total_rows == 0) return 1;
+    const int vec = (int)(kv_width * 2 / 16);
+    const unsigned grid = (unsigned)((total_rows + kCopyWarps - 1) / kCopyWarps);
+    auto *kp = static_cast<uint4 *>(layer->key_pool);
+    auto *vp = static_cast<uint4 *>(layer->value_pool);
+    auto *kr = static_cast<uint4 *>(const_cast<void *>(krows));
+    auto *vr = static_cast<uint4 *>(const_cast<void *>(vrows));
+    const int shift = block_shift_of(layer->block_size);
+#define PKV_ROWS(V)                                                                          \
+    kv_rows_kernel<TO_POOL, V><<<grid, kCopyWarps * 32, 0, (cudaStream_t)stream>>>(          \
+        kp, vp, kr, vr, batch->block_tables, (int32_t)batch->table_stride, batch->seq_lens, \
+        offsets, (int)batch->batch, (int32_t)total_rows, vec, (int)layer->block_size, shift, \
+        (uint32_t)layer->block_count, tail)
+    switch (vec) {
+        case 32: PKV_ROWS(1); break;    // 512 B rows (e.g. 2 heads x 128)
+        case 64: PKV_ROWS(2); break;
+        case 128: PKV_ROWS(4); break;   // 2 KiB rows (8 heads x 128)
+        case 256: PKV_ROWS(8); break;
+        default: PKV_ROWS(0); break;
+    }
+#undef PKV_ROWS
+    const cudaError_t st = cudaGetLastError();
+    if (st != cudaSuccess) {
+        pkv_internal_set_error(error, cap, "%s: launch failed: %s", what, cudaGetErrorString(st));
+        return 0;
+    }
+    return 1;
+}
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" {
+
+void pkv_internal_set_error(char *error, size_t capacity, const char *fmt, ...) {
+    if (error == nullptr || capacity == 0) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(error, capacity, fmt, ap);
+    va_end(ap);
+}
+
+int pkv_kv_append(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
+                  const void *key_rows, const void *value_rows, size_t total_rows,
+                  PkvStream stream, char *error, size_t error_capacity) {
+    return pkv::launch_rows<true>(layer, batch, row_offsets, key_rows, value_rows, total_rows,
+                                  true, stream, error, error_capacity, "pkv_kv_append");
+}
+
+int pkv_kv_import(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
+                  const void *key_rows, const void *value_rows, size_t total_rows,
+                  PkvStream stream, char *error, size_t error_capacity) {
+    return pkv::launch_rows<true>(layer, batch, row_offsets, key_rows, value_rows, total_rows,
+                                  false, stream, error, error_capacity, "pkv_kv_import");
+}
+
+int pkv_kv_gather(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
+                  void *key_out, void *value_out, size_t total_rows, PkvStream stream,
+                  char *error, size_t error_capacity) {
+    return pkv::launch_rows<false>(layer, batch, row_offsets, key_out, value_out, total_rows,
+                                   false, stream, error, error_capacity, "pkv_kv_gather");
+}
+
+int pkv_internal_apply_patches(uint32_t *table, size_t table_stride, size_t table_rows,
+                               const PkvTablePatch *patches, size_t count, PkvStream stream) {
+    if (count == 0) return 1;
+    const unsigned grid = (unsigned)((count + 255) / 256);
+    pkv::apply_patches_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        table, (int64_t)table_stride, (int64_t)table_rows, patches, (int64_t)count);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+// Reads and clears this unit's fault word on the current device.
+int pkv_internal_take_copy_fault(uint32_t *code) {
+    uint32_t zero = 0;
+    if (cudaMemcpyFromSymbol(code, pkv::g_copy_fault, sizeof(uint32_t)) != cudaSuccess) return 0;
+    return cudaMemcpyToSymbol(pkv::g_copy_fault, &zero, sizeof(uint32_t)) == cudaSuccess;
+}
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+/*
+ * pkv_internal.h -- declarations shared between the C11 host layer
+ * (pkv_pool.c, paged_kv_cache.c) and the CUDA translation units.  Not part of
+ * the public ABI in include/pkv_b200.h.
+ */
+#ifndef PKV_INTERNAL_H
+#define PKV_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "pkv_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One new page-table entry: table[row * stride + index] = page. */
+typedef struct {
+    uint32_t row;
+    uint32_t index;
+    uint32_t page;
+    uint32_t pad;
+} PkvTablePatch;
+
+/* Applies `count` patches (device array) to a padded device table. */
+int pkv_internal_apply_patches(uint32_t *table, size_t table_stride,
+                               size_t table_rows, const PkvTablePatch *patches,
+                               size_t count, PkvStream stream);
+
+/* Copies page ids [from, page_count) of `sequence` into dst and reports the
+ * full page count; 0 for an unknown handle or a too-small capacity.  One
+ * lock round trip, so the host layer uploads only the table's new tail;
+ * *shrink_epoch changes whenever pages were removed from the table. */
+int pkv_internal_copy_table_tail(TensorPagedKVCache *cache,
+                                 TensorPagedKVSequence sequence, size_t from,
+                                 uint32_t *dst, size_t capacity,
+                                 size_t *page_count, size_t *length,
+                                 uint32_t *shrink_epoch);
+
+/* Read and clear the fault word of one kernel translation unit. */
+int pkv_internal_take_copy_fault(uint32_t *code);
+int pkv_internal_take_decode_fault(uint32_t *code);
+int pkv_internal_take_prefill_fault(uint32_t *code);
+
+/* Writes a message into a caller error buffer (NULL-safe). */
+void pkv_internal_set_error(char *error, size_t capacity, const char *fmt, ...);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,126 @@
+"""The C ABI boundary, checked without a GPU: the library loads, exports every
+function include/*.h declares (and the Python view binds them all), rejects
+bad arguments with a 0 result and a message before touching the device, and
+neither links nor names the oracle."""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+import inference_c_b200 as P
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+
+
+def _declared_functions() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"^typedef[^;]*;", "", text, flags=re.M | re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w\s\*]*?\b(\w+)\s*\(", text, flags=re.M):
+            name = m.group(1)
+            if name not in {"if", "return", "typedef", "sizeof"}:
+                names.add(name)
+    return names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_functions()
+    assert len(declared) >= 30
+    out = subprocess.run(["nm", "-D", "--defined-only", str(P.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = declared - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    assert declared <= set(P.EXPORTS), sorted(declared - set(P.EXPORTS))
+
+
+def test_product_does_not_link_or_name_the_oracle(lib):
+    out = subprocess.run(["nm", "-D", str(P.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    assert "orc_" not in out and "ref_job" not in out
+    needed = subprocess.run(["readelf", "-d", str(P.LIB_PATH)], capture_output=True, text=True,
+                            check=True).stdout
+    assert "oracle" not in needed
+    for f in (ROOT / "inference_c_b200").rglob("*"):
+        if f.suffix in {".py", ".c", ".cu", ".cuh", ".h"}:
+            assert "oracle" not in f.read_text().replace("oracle-free", ""), f
+
+
+def test_sm100a_only(lib):
+    """Kernels are built for sm_100a and nothing else."""
+    out = subprocess.run(["cuobjdump", "--list-elf", str(P.LIB_PATH)], capture_output=True,
+                         text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_\w+", out.stdout))
+    assert arches == {"sm_100a"}, arches
+
+
+def _err():
+    return ctypes.create_string_buffer(256)
+
+
+def test_kernel_entry_points_reject_bad_arguments(lib):
+    e = _err()
+    assert lib.pkv_kv_append(None, None, None, None, None, 0, None, e, len(e)) == 0
+    assert b"null" in e.value
+    layer = P.PkvPagedLayer(16, 16, 16, 4, 2, 128, 7)  # bad dtype
+    batch = P.PkvBatch(16, 4, 16, 1)
+    e = _err()
+    assert lib.pkv_kv_append(ctypes.byref(layer), ctypes.byref(batch), None, 16, 16, 1, None, e,
+                             len(e)) == 0
+    assert b"dtype" in e.value
+    layer.dtype = P.PKV_DTYPE_F16
+    e = _err()
+    assert lib.pkv_kv_append(ctypes.byref(layer), ctypes.byref(batch), None, 16, 16, 2, None, e,
+                             len(e)) == 0  # one row per sequence needs total_rows == batch
+    assert b"total_rows" in e.value
+    e = _err()
+    assert lib.pkv_kv_append(ctypes.byref(layer), ctypes.byref(batch), None, 24, 16, 1, None, e,
+                             len(e)) == 0
+    assert b"aligned" in e.value
+    # decode: GQA group 3 and head_dim 96 are rejected up front
+    e = _err()
+    assert lib.pkv_paged_decode(ctypes.byref(layer), ctypes.byref(batch), 6, 16,
+                                ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256, 1 << 20,
+                                None, e, len(e)) == 0
+    assert b"q_heads/kv_heads" in e.value
+    layer.head_dim = 96
+    e = _err()
+    assert lib.pkv_paged_decode(ctypes.byref(layer), ctypes.byref(batch), 4, 16,
+                                ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256, 1 << 20,
+                                None, e, len(e)) == 0
+    assert b"head_dim" in e.value
+    layer.head_dim = 128
+    e = _err()
+    assert lib.pkv_paged_decode(ctypes.byref(layer), ctypes.byref(batch), 4, 16,
+                                ctypes.c_float(float("nan")), 16, P.PKV_DTYPE_F32, 64, 0, 256,
+                                1 << 20, None, e, len(e)) == 0
+    e = _err()
+    assert lib.pkv_paged_decode(ctypes.byref(layer), ctypes.byref(batch), 4, 16,
+                                ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256, 8, None, e,
+                                len(e)) == 0
+    assert b"workspace" in e.value
+    e = _err()
+    assert lib.pkv_step_begin(None, None, None, None, 0, None, e, len(e)) == 0
+    assert lib.pkv_step_end(None, 1, e, len(e)) == 0
+
+
+def test_workspace_size_is_monotonic(lib):
+    small = lib.pkv_decode_workspace_bytes(1, 8, 64, 512, 0)
+    big = lib.pkv_decode_workspace_bytes(32, 32, 128, 4096, 0)
+    bigger = lib.pkv_decode_workspace_bytes(256, 32, 128, 32768, 0)
+    assert 0 < small < big < bigger
+    assert bigger % 256 == 0
+
+
+def test_python_view_fails_loudly_without_library(monkeypatch, tmp_path):
+    monkeypatch.setattr(P, "LIB_PATH", tmp_path / "missing.so")
+    monkeypatch.setattr(P, "_lib", None)
+    with pytest.raises(RuntimeError, match="no fallback"):
+        P.load()

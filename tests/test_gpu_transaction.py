@@ -1,0 +1,188 @@
+"""The C11 host layer on the GPU: a device pool attached to a cache through
+the SDK's backend hook, the batch step transaction (begin_decode, length
+check, reserve, device table upload, commit or rollback, end_decode), prefix
+import through a step, and decode steps checked against the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import inference_c_b200 as P
+from inference_c_b200 import workloads as W
+from tests.gpu_cases import check_close, to_device_bits, to_host_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(n_seq=3, pages=64, max_pages=32, layers=2, kvh=2, d=128):
+    cache = P.PagedKVCache(16, pages, 8)
+    pool = P.PagedPool(cache, 0, P.PKV_DTYPE_F16, layers, kvh, d, 8, max_pages)
+    seqs = [cache.sequence_create() for _ in range(n_seq)]
+    return cache, pool, seqs
+
+
+def dump_pool(layer: P.PkvPagedLayer, cuda):
+    """Whole K and V pools in physical order, read with an identity table."""
+    import torch
+    pages = layer.block_count
+    rows = pages * layer.block_size
+    kv = layer.kv_heads * layer.head_dim
+    ident = torch.arange(pages, dtype=torch.int32, device=cuda).view(1, -1)
+    lens = torch.tensor([rows], dtype=torch.int32, device=cuda)
+    offs = torch.tensor([0, rows], dtype=torch.int32, device=cuda)
+    k = torch.empty(rows, kv, dtype=torch.float16, device=cuda)
+    v = torch.empty_like(k)
+    P.kv_gather(layer, P.make_batch(ident, lens), k, v, offs)
+    torch.cuda.synchronize()
+    return to_host_bits(k), to_host_bits(v)
+
+
+def _tables(cache, seqs, width):
+    tab = np.zeros((len(seqs), width), np.uint32)
+    for b, s in enumerate(seqs):
+        t = cache.block_table(s)
+        tab[b, :len(t)] = t
+    return tab
+
+
+def test_pool_attaches_once_and_frees_with_cache(lib, cuda):
+    cache, pool, _ = _setup()
+    assert lib.pkv_pool_from_cache(cache.handle) == pool.handle
+    with pytest.raises(P.PkvError, match="already has a CUDA pool"):
+        P.PagedPool(cache, 0, P.PKV_DTYPE_F16, 1, 2, 128, 8, 32)
+    layer = pool.layer(1)
+    assert layer.block_count == 64 and layer.kv_heads == 2 and layer.head_dim == 128
+    k, v = dump_pool(layer, cuda)
+    assert not k.any() and not v.any()  # pools start zeroed
+    cache.free()  # runs the pool's destroy callback
+
+
+def test_prefix_import_then_decode_steps(lib, oracle_mod, cuda):
+    import torch
+    kvh, d, qh, layers = 2, 128, 8, 2
+    cache, pool, seqs = _setup(kvh=kvh, d=d, layers=layers)
+    past = [37, 16, 90]
+    for r in range(1, 7):  # interleaved reservations: fragmented tables
+        for s, L in zip(seqs, past):
+            cache.reserve(s, min(L, 16 * r))
+    kv = kvh * d
+    host_k = [W.normal_bits(40 + l, (sum(past), kv), "f16", stream=1) for l in range(layers)]
+    host_v = [W.normal_bits(40 + l, (sum(past), kv), "f16", stream=2) for l in range(layers)]
+    # prefix import: current length 0, past given, every token new
+    pool.step_begin(seqs, past, past_lengths=past)
+    for l in range(layers):
+        P.kv_import(pool.layer(l), pool.step_batch(), to_device_bits(host_k[l], "f16", cuda),
+                    to_device_bits(host_v[l], "f16", cuda), pool.step_row_offsets())
+    pool.step_end(True)
+    assert [cache.length(s) for s in seqs] == past
+    rows = 64 * 16
+    mk = [np.zeros((rows, kv), np.uint16) for _ in range(layers)]
+    mv = [np.zeros((rows, kv), np.uint16) for _ in range(layers)]
+    tab = _tables(cache, seqs, 32)
+    assert len({int(x) for x in tab[tab > 0]}) == int((tab > 0).sum())
+    offs = np.concatenate([[0], np.cumsum(past)]).astype(np.int32)
+    for l in range(layers):
+        oracle_mod.kv_rows(mk[l], mv[l], 16, tab, np.array(past), offs, host_k[l].copy(),
+                           host_v[l].copy(), to_pool=True, tail=False)
+    lengths = list(past)
+    ws = P.decode_workspace(3, qh, d, 200, device=cuda)
+    out = torch.empty(3, qh, d, dtype=torch.float32, device=cuda)
+    for step in range(20):  # crosses a page boundary for every sequence
+        pool.step_begin(seqs, [1, 1, 1])
+        batch = pool.step_batch()
+        lengths = [L + 1 for L in lengths]
+        tab = _tables(cache, seqs, 32)
+        for l in range(layers):
+            nk = W.normal_bits(1000 + step * 7 + l, (3, kv), "f16", stream=3)
+            nv = W.normal_bits(1000 + step * 7 + l, (3, kv), "f16", stream=4)
+            q = W.normal_bits(1000 + step * 7 + l, (3, qh, d), "f16", stream=5)
+            layer = pool.layer(l)
+            P.kv_append(layer, batch, to_device_bits(nk, "f16", cuda),
+                        to_device_bits(nv, "f16", cuda))
+            P.paged_decode(layer, batch, to_device_bits(q, "f16", cuda), out,
+                           float(1 / np.sqrt(d)), 200, ws)
+            oracle_mod.kv_rows(mk[l], mv[l], 16, tab, np.array(lengths), None, nk.copy(),
+                               nv.copy(), to_pool=True, tail=True)
+            torch.cuda.synchronize()
+            want = oracle_mod.paged_decode(q, "f16", mk[l], mv[l], kvh, d, 16, tab,
+                                           np.array(lengths), float(1 / np.sqrt(d)))
+            check_close(out.cpu().numpy(), want, f"step {step} layer {l}")
+        pool.step_end(True)
+    assert [cache.length(s) for s in seqs] == lengths
+    for l in range(layers):
+        k, v = dump_pool(pool.layer(l), cuda)
+        assert np.array_equal(k, mk[l]) and np.array_equal(v, mv[l])
+    assert P.device_fault(0) == 0
+    cache.free()
+
+
+def test_step_rollback_and_atomic_failure(lib, cuda):
+    cache, pool, seqs = _setup(pages=8, max_pages=8)
+    for s in seqs:
+        cache.reserve(s, 16)
+        cache.set_length(s, 16)
+    free0 = cache.free_blocks()
+    # explicit rollback: lengths and pages come back, locks are released
+    pool.step_begin(seqs, [20, 1, 17])
+    assert cache.free_blocks() == free0 - 3
+    pool.step_end(False)
+    assert cache.free_blocks() == free0 and [cache.length(s) for s in seqs] == [16, 16, 16]
+    assert all(cache.begin_decode(s) for s in seqs)
+    for s in seqs:
+        cache.end_decode(s)
+    # out of pages on the third sequence: nothing changes anywhere
+    with pytest.raises(P.PkvError, match="out of pages"):
+        pool.step_begin(seqs, [16, 16, 64])
+    assert cache.free_blocks() == free0 and [cache.length(s) for s in seqs] == [16, 16, 16]
+    # a sequence already decoding fails the whole step; the others stay unlocked
+    assert cache.begin_decode(seqs[1])
+    with pytest.raises(P.PkvError, match="already decoding"):
+        pool.step_begin(seqs, [1, 1, 1])
+    cache.end_decode(seqs[1])
+    assert cache.begin_decode(seqs[0])
+    cache.end_decode(seqs[0])
+    # the SDK's rule: the current length must be 0 or equal to past
+    with pytest.raises(P.PkvError, match="length mismatch"):
+        pool.step_begin(seqs, [1, 1, 1], past_lengths=[16, 15, 16])
+    assert cache.free_blocks() == free0
+    # one open step at a time; release is refused while the step holds the lock
+    pool.step_begin(seqs, [1, 1, 1])
+    with pytest.raises(P.PkvError, match="already open"):
+        pool.step_begin(seqs, [1, 1, 1])
+    assert cache.release(seqs[0]) == 0
+    pool.step_end(True)
+    assert [cache.length(s) for s in seqs] == [17, 17, 17]
+    cache.free()
+
+
+def test_truncation_resends_table_rows(lib, oracle_mod, cuda):
+    """After set_length drops pages and another sequence takes them, the
+    next step's pages at the same logical indices differ; the device table
+    must follow or appends would land in the other sequence's pages."""
+    import torch
+    cache, pool, seqs = _setup(n_seq=2, pages=16, max_pages=8, layers=1, kvh=1, d=64)
+    a, b = seqs
+    pool.step_begin([a, b], [40, 40])
+    pool.step_end(True)
+    cache.set_length(a, 10)           # a drops pages 1, 2
+    cache.reserve(b, 80)              # b takes them
+    pool.step_begin([a, b], [30, 1])  # a gets fresh pages at indices 1, 2
+    batch = pool.step_batch()
+    tab = _tables(cache, [a, b], 8)
+    lens = np.array([40, 41])
+    kv = 64
+    krow = W.normal_bits(5, (31, kv), "f16", stream=1)
+    vrow = W.normal_bits(5, (31, kv), "f16", stream=2)
+    offs = np.array([0, 30, 31], np.int32)
+    P.kv_append(pool.layer(0), batch, to_device_bits(krow, "f16", cuda),
+                to_device_bits(vrow, "f16", cuda), pool.step_row_offsets())
+    torch.cuda.synchronize()
+    mk = np.zeros((16 * 16, kv), np.uint16)
+    mv = np.zeros((16 * 16, kv), np.uint16)
+    oracle_mod.kv_rows(mk, mv, 16, tab, lens, offs, krow.copy(), vrow.copy(), to_pool=True,
+                       tail=True)
+    k, v = dump_pool(pool.layer(0), cuda)
+    assert np.array_equal(k, mk) and np.array_equal(v, mv)
+    pool.step_end(True)
+    assert P.device_fault(0) == 0
+    cache.free()
