@@ -302,7 +302,7 @@ def run_ours(args) -> None:
     for b in picks:  # one page at a time, sequences in seeded random order
         have[b] += 1
         assert cache.reserve(seqs[b], int(min(lengths[b], 16 * have[b])))
-    pool.step_begin(seqs, lengths.tolist(), past_lengths=lengths.tolist())
+    pool.step_begin(seqs, lengths.tolist())  # the whole context is this step's new rows
     batch = pool.step_batch()
     layer = pool.layer(0)
     gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)

@@ -20,9 +20,14 @@
 // exp(m_i - m_max)); the result equals softmax(q.K^T * scale) . V as computed
 // by tensor_sdpa_f32 (attention.c:212-406) up to FP32 rounding.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cudaTypedefs.h>
 
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_sm100.cuh"
 
 namespace pkv {
 namespace {
@@ -80,7 +85,7 @@ size_t smem_bytes(int batch) {
 
 template <int HD, int G, typename T, typename OT>
 __global__ void __launch_bounds__(kThreads, (G >= 8 ? 1 : 2))
-paged_decode_kernel(const DecodeArgs a) {
+paged_decode_simt_kernel(const DecodeArgs a) {
     using C = Cfg<HD, G>;
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr size_t kKV = 2u * kStages * C::STAGE * sizeof(T);
@@ -362,9 +367,9 @@ paged_decode_kernel(const DecodeArgs a) {
                 pm[1] = l_s[tid];
             }
         }
-        __threadfence();
         __syncthreads();
         if (tid == 0) {
+            __threadfence();  // publishes the whole block's partials (bar.sync is cumulative)
             const uint32_t ticket = atomicAdd(a.counters + (int64_t)b * a.kv_heads + g, 1u);
             misc[0] = ticket == (uint32_t)(nchunks - 1);
         }
@@ -402,6 +407,573 @@ paged_decode_kernel(const DecodeArgs a) {
     }
 }
 
+size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
+
+// ---------------------------------------------------------------------------
+// tcgen05 path (head_dim 128, page sizes 16/32/64/128, q_heads/kv_heads <= 16)
+//
+// One persistent CTA per SM, 192 threads, warp-specialised:
+//   warp 0     producer: stages the piece's query rows as the B operand and
+//              TMA-loads every page of a 128-token tile straight from the pool
+//              (one 2-D box per page and 64-column half: no gather copy),
+//              3-deep ring of 64 KiB (K 32 KiB + V 32 KiB) stages;
+//   warp 1     one thread issues tcgen05.mma:
+//                S^T[128 tok][16] = K[128 tok][128] . Q^T         (TMEM, f32)
+//                O^T[128 d][PN]  = V^T[128 d][128 tok] . P^T       (TMEM, f32)
+//              M = 128 tokens / dims, N = the query heads of the GQA group
+//              (zero-padded), so each page byte feeds every head once;
+//   warps 2-5  softmax / merge group: thread i owns token i of S^T (and dim i
+//              of O^T); per tile it takes the block-wide running max per head,
+//              writes P = exp2(s - m) to shared memory, zeroes V rows past the
+//              length, and folds the tile's O into FP32 registers with the
+//              running-max correction.
+// P is written as two storage-dtype halves, hi = round(p) in B rows [0, G)
+// and lo = round(p - hi) in rows [PN/2, PN/2 + G), so the one PV MMA returns
+// O_hi and O_lo side by side and their sum carries ~22 bits of P (a single
+// FP16 P costs ~1% relative error on small outputs).
+//
+// Work split ("stream-K"): the 128-token tiles of every (sequence, KV head)
+// segment, sequence-major, form one stream of T tiles and CTA i of n takes
+// tiles [T*i/n, T*(i+1)/n), so every CTA streams the same number of bytes
+// whatever the length mix.  A segment inside one CTA's range is finished
+// there; a segment cut by range ends leaves one partial (m, l, O) per piece,
+// in slot 0 (the CTA's first piece) or slot 1 (its last piece).  The last CTA
+// to finish a piece of such a segment merges them (atomic ticket), unless one
+// segment can span more than kInKernelMergeMax CTAs (few KV heads, one long
+// sequence); then pkv_tc_merge_kernel, one CTA per (sequence, query head),
+// merges after the decode kernel.
+// ---------------------------------------------------------------------------
+constexpr int kTcThreads = 192;
+constexpr int kTcTile = 128;
+constexpr int kTcStages = 3;
+constexpr int kTcMaxBatch = 1024;
+constexpr int kTcMaxGrid = 256;
+constexpr int kInKernelMergeMax = 32;
+constexpr uint32_t kTcStageBytes = 65536;
+constexpr uint32_t kTcHalf = 16384;       // 128 rows x 128 bytes
+constexpr uint32_t kTcQOff = kTcStages * kTcStageBytes;
+constexpr uint32_t kTcPOff = kTcQOff + 2 * 4096;
+constexpr uint32_t kTcPBuf = 8192;        // one P^T tile of up to 32 rows
+constexpr uint32_t kTcBarOff = kTcPOff + 2 * kTcPBuf;
+constexpr uint32_t kTcMiscOff = kTcBarOff + 256;
+constexpr uint32_t kTcPrefixOff = kTcMiscOff + 2048;
+constexpr uint32_t kTcTmemCols = 128;
+
+size_t tc_smem_bytes(int batch) { return kTcPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
+
+struct TcArgs {
+    const uint32_t *tables;
+    const int32_t *seq_lens;
+    const void *query;
+    void *out;
+    uint32_t *counters;     // [batch * kv_heads] tickets of the in-kernel merge
+    float *part_ml;         // [kTcMaxGrid][2 slots][16 heads][m, l]
+    float *part_o;          // [kTcMaxGrid][2 slots][16 heads][128]
+    int32_t *tile_prefix;   // [batch + 1] copy of the tile prefix for the merge kernel
+    int32_t table_stride;
+    int32_t batch;
+    int32_t kv_heads;
+    int32_t block_size;
+    uint32_t block_count;
+    float scale_log2;
+    int32_t merge_in_kernel;
+};
+
+struct TcWorkspace {
+    size_t counters, ml, o, prefix, total;
+};
+
+TcWorkspace tc_workspace(size_t batch, size_t kv_heads) {
+    TcWorkspace w;
+    w.counters = 0;
+    w.ml = round_up(batch * kv_heads * sizeof(uint32_t), 256);
+    w.o = w.ml + round_up((size_t)kTcMaxGrid * 2 * 16 * 2 * sizeof(float), 256);
+    w.prefix = w.o + round_up((size_t)kTcMaxGrid * 2 * 16 * 128 * sizeof(float), 256);
+    w.total = w.prefix + round_up((batch + 1) * sizeof(int32_t), 256);
+    return w;
+}
+
+__device__ __forceinline__ int64_t range_start(int cta, int ncta, int64_t T) {
+    return T * cta / ncta;
+}
+// The CTA whose range holds tile t.
+__device__ __forceinline__ int cta_of_tile(int64_t t, int ncta, int64_t T) {
+    return (int)(((t + 1) * ncta - 1) / T);
+}
+// Partial slot a CTA used for the piece of the segment starting at tile `seg`.
+__device__ __forceinline__ int piece_slot(int cta, int64_t seg, int ncta, int64_t T) {
+    return range_start(cta, ncta, T) < seg ? 1 : 0;
+}
+
+// Exclusive prefix of tiles per sequence times kv_heads (0 for empty ones).
+__device__ void build_tile_prefix(const TcArgs &a, int *prefix, int *scratch) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int per = (a.batch + nthr - 1) / nthr;
+    int local = 0;
+    for (int k = 0; k < per; ++k) {
+        const int b = tid * per + k;
+        if (b < a.batch)
+            local += (max(0, __ldg(a.seq_lens + b)) + kTcTile - 1) / kTcTile * a.kv_heads;
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += scratch[w];
+    int run = before + incl - local;
+    for (int k = 0; k < per; ++k) {
+        const int b = tid * per + k;
+        if (b < a.batch) {
+            prefix[b] = run;
+            run += (max(0, __ldg(a.seq_lens + b)) + kTcTile - 1) / kTcTile * a.kv_heads;
+        }
+    }
+    if (tid == nthr - 1) prefix[a.batch] = before + incl;
+}
+
+// One contiguous run of tiles of one (sequence, KV head) segment.
+struct Piece {
+    int b, g, k0, k1, nt;
+    int64_t seg;  // stream index of the segment's first tile
+};
+
+__device__ __forceinline__ Piece piece_at(int64_t t, int64_t end, const int *prefix,
+                                          const TcArgs &a) {
+    Piece P;
+    int lo = 0, hi = a.batch - 1;  // last sequence whose first tile is <= t
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    P.b = lo;
+    P.nt = (prefix[lo + 1] - prefix[lo]) / a.kv_heads;
+    const int64_t within = t - prefix[lo];
+    P.g = (int)(within / P.nt);
+    P.k0 = (int)(within - (int64_t)P.g * P.nt);
+    P.seg = prefix[lo] + (int64_t)P.g * P.nt;
+    P.k1 = (int)min((int64_t)P.nt, (int64_t)P.k0 + (end - t));
+    return P;
+}
+
+template <typename T>
+struct IsBf16 { static constexpr bool value = false; };
+template <>
+struct IsBf16<__nv_bfloat16> { static constexpr bool value = true; };
+
+// Merges the partials of head h of segment (b, g): m/l of every piece are
+// staged in shared memory (`stage`, 3 floats per piece), then each thread
+// sums its output element over the pieces.  `tid`/`nthr` are the
+// participating threads; `sync` is their barrier.
+template <typename OT, typename Sync>
+__device__ __forceinline__ void merge_head(const TcArgs &a, int h, int64_t seg, int nt, int ncta,
+                                           int64_t T, int tid, int nthr, float *stage, int cap,
+                                           OT *outh, Sync sync) {
+    const int first = cta_of_tile(seg, ncta, T);
+    const int np = cta_of_tile(seg + nt - 1, ncta, T) - first + 1;
+    if (np > cap) {  // cannot happen with the host's choice of merge mode
+        if (tid == 0) record_fault(&g_decode_fault, kFaultPositionOutOfRange);
+        return;
+    }
+    for (int c = tid; c < np; c += nthr) {
+        const int cta = first + c;
+        const int k = piece_slot(cta, seg, ncta, T);
+        const float *ml = a.part_ml + (((int64_t)cta * 2 + k) * 16 + h) * 2;
+        stage[3 * c] = __ldcg(ml);
+        stage[3 * c + 1] = __ldcg(ml + 1);
+        stage[3 * c + 2] = __int_as_float(k);
+    }
+    sync();
+    float mx = -INFINITY;
+    for (int c = 0; c < np; ++c) mx = fmaxf(mx, stage[3 * c]);
+    float lt = 0.f, ot = 0.f;
+    for (int d = tid; d < 128; d += nthr) {
+        lt = 0.f;
+        ot = 0.f;
+        int c = 0;
+        for (; c + 4 <= np; c += 4) {  // four independent loads in flight
+            float v[4], f[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int cta = first + c + i;
+                const int k = __float_as_int(stage[3 * (c + i) + 2]);
+                v[i] = __ldcg(a.part_o + (((int64_t)cta * 2 + k) * 16 + h) * 128 + d);
+                const float mc = stage[3 * (c + i)];
+                f[i] = mc == -INFINITY ? 0.f : exp2f(mc - mx);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lt += stage[3 * (c + i) + 1] * f[i];
+                ot += v[i] * f[i];
+            }
+        }
+        for (; c < np; ++c) {
+            const int cta = first + c;
+            const int k = __float_as_int(stage[3 * c + 2]);
+            const float mc = stage[3 * c];
+            const float f = mc == -INFINITY ? 0.f : exp2f(mc - mx);
+            lt += stage[3 * c + 1] * f;
+            ot += __ldcg(a.part_o + (((int64_t)cta * 2 + k) * 16 + h) * 128 + d) * f;
+        }
+        outh[d] = from_f32<OT>(lt > 0.f ? ot / lt : 0.f);
+    }
+    sync();
+}
+
+template <int G, typename T, typename OT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap) {
+    using namespace sm100;
+    constexpr int GN = G <= 4 ? 4 : G;  // S^T columns read per thread
+    constexpr int PN = G <= 8 ? 16 : 32;  // P^T rows (= O^T columns): hi and lo halves
+    constexpr int LO = PN / 2;
+    constexpr uint32_t kPChunk = PN * 128;  // bytes of one 64-token column chunk of P^T
+    constexpr uint32_t kIdescQK = idesc_f16(128, 16, IsBf16<T>::value, false, false);
+    constexpr uint32_t kIdescPV = idesc_f16(128, PN, IsBf16<T>::value, true, false);
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *sm = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kTcBarOff);
+    uint64_t *full = bars, *empty = bars + 3, *s_full = bars + 6, *s_empty = bars + 8;
+    uint64_t *p_full = bars + 10, *o_full = bars + 12, *o_empty = bars + 14;
+    uint64_t *q_full = bars + 16, *q_empty = bars + 18;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kTcMiscOff);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kTcMiscOff + 4);
+    int *ticket = reinterpret_cast<int *>(sm + kTcMiscOff + 8);
+    int *scan = reinterpret_cast<int *>(sm + kTcMiscOff + 32);    // 8 ints
+    float *red = reinterpret_cast<float *>(sm + kTcMiscOff + 64);  // [2][4][16]
+    float *lred = red + 128;                                        // [4][16]
+    float *mstage = lred + 64;                                      // 3 * kInKernelMergeMax
+    int *prefix = reinterpret_cast<int *>(sm + kTcPrefixOff);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], 128);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_empty[i], 128);
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    // Q and P tiles: rows past the group stay zero for the whole kernel.
+    for (int i = tid; i < (int)(2 * 4096 + 2 * kTcPBuf) / 16; i += kTcThreads)
+        reinterpret_cast<uint4 *>(sm + kTcQOff)[i] = make_uint4(0, 0, 0, 0);
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTcTmemCols);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        tma_prefetch_desc(&kmap);
+        tma_prefetch_desc(&vmap);
+    }
+    build_tile_prefix(a, prefix, scan);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int64_t total_tiles = prefix[a.batch];
+    // CTAs past the tile count idle, so every working CTA owns >= 1 tile and
+    // the CTAs spanned by a segment are exactly its pieces.
+    const int ncta = (int)min((int64_t)gridDim.x, max(total_tiles, (int64_t)1));
+    const bool works = (int)blockIdx.x < ncta && total_tiles > 0;
+    const int64_t my_start = works ? range_start(blockIdx.x, ncta, total_tiles) : 0;
+    const int64_t my_end = works ? range_start(blockIdx.x + 1, ncta, total_tiles) : 0;
+    const int q_heads = a.kv_heads * G;
+    uint32_t *fault = &g_decode_fault;
+    if (blockIdx.x == 0 && a.tile_prefix != nullptr)
+        for (int b = tid; b <= a.batch; b += kTcThreads) a.tile_prefix[b] = prefix[b];
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        uint32_t j = 0, qi = 0;
+        bool ok = true;
+        for (int64_t t = my_start; ok && t < my_end;) {
+            const Piece P = piece_at(t, my_end, prefix, a);
+            t += P.k1 - P.k0;
+            const int L = __ldg(a.seq_lens + P.b);
+            if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) break;
+            unsigned char *qb = sm + kTcQOff + (qi & 1) * 4096;
+            const T *qsrc = static_cast<const T *>(a.query) +
+                            ((int64_t)P.b * q_heads + (int64_t)P.g * G) * 128;
+            for (int idx = lane; idx < G * 16; idx += 32) {
+                const int h = idx >> 4, c16 = idx & 15;
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qsrc + h * 128 + c16 * 8));
+                *reinterpret_cast<uint4 *>(qb + sw128_offset(h, c16 * 8, 2048)) = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_full[qi & 1]);
+            const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
+            for (int k = P.k0; k < P.k1; ++k, ++j) {
+                const int stage = (int)(j % kTcStages);
+                if (!mbar_wait(&empty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
+                    ok = false;
+                    break;
+                }
+                const int ts = k * kTcTile;
+                const int te = min(L, ts + kTcTile);
+                const int p0 = ts / a.block_size;
+                const int np = (te - ts + a.block_size - 1) / a.block_size;
+                uint32_t pid = 0;
+                bool good = false;
+                if (lane < np) {
+                    const int pi = p0 + lane;
+                    if (pi < a.table_stride) {
+                        pid = __ldg(trow + pi);
+                        good = pid < a.block_count;
+                    }
+                    if (!good) record_fault(fault, kFaultPageOutOfRange);
+                }
+                const unsigned mask = __ballot_sync(0xffffffffu, good);
+                if (lane == 0)
+                    mbar_arrive_expect_tx(&full[stage], (uint32_t)__popc(mask) * a.block_size * 512u);
+                __syncwarp();
+                if (good) {
+                    unsigned char *st = sm + stage * kTcStageBytes;
+                    const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
+                    const int32_t y = (int32_t)pid * a.block_size;
+                    const int32_t x = P.g * 128;
+                    tma_load_2d(st + ro, &kmap, &full[stage], x, y);
+                    tma_load_2d(st + kTcHalf + ro, &kmap, &full[stage], x + 64, y);
+                    tma_load_2d(st + 2 * kTcHalf + ro, &vmap, &full[stage], x, y);
+                    tma_load_2d(st + 3 * kTcHalf + ro, &vmap, &full[stage], x + 64, y);
+                }
+            }
+            ++qi;
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            uint32_t j = 0, qi = 0;
+            bool ok = true;
+            for (int64_t t = my_start; ok && t < my_end;) {
+                const Piece P = piece_at(t, my_end, prefix, a);
+                t += P.k1 - P.k0;
+                if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag, fault)) break;
+                const uint32_t qaddr = smem_u32(sm + kTcQOff + (qi & 1) * 4096);
+                for (int k = P.k0; k < P.k1; ++k, ++j) {
+                    const int stage = (int)(j % kTcStages);
+                    const uint32_t buf = j & 1, par = (j >> 1) & 1;
+                    if (!mbar_wait(&full[stage], (j / kTcStages) & 1, abort_flag, fault) ||
+                        !mbar_wait(&s_empty[buf], par ^ 1, abort_flag, fault)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t kaddr = smem_u32(sm + stage * kTcStageBytes);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_desc(kaddr + (kk >> 2) * kTcHalf + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = sw128_desc(qaddr + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024);
+                        mma_f16_ss(tmem + buf * 16, ad, bd, kIdescQK, kk > 0);
+                    }
+                    mma_commit(&s_full[buf]);
+                    if (k == P.k1 - 1) mma_commit(&q_empty[qi & 1]);
+                    if (!mbar_wait(&p_full[buf], par, abort_flag, fault) ||
+                        !mbar_wait(&o_empty[buf], par ^ 1, abort_flag, fault)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t vaddr = kaddr + 2 * kTcHalf;
+                    const uint32_t paddr = smem_u32(sm + kTcPOff + buf * kTcPBuf);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_desc(vaddr + kk * 2048, kTcHalf, 1024);
+                        const uint64_t bd = sw128_desc(paddr + (kk >> 2) * kPChunk + (kk & 3) * 32, 16, 1024);
+                        mma_f16_ss(tmem + 32 + buf * PN, ad, bd, kIdescPV, kk > 0);
+                    }
+                    mma_commit(&o_full[buf]);
+                    mma_commit(&empty[stage]);
+                }
+                ++qi;
+            }
+        }
+        __syncwarp();
+    } else {
+        // --------------------------- softmax / merge ---------------------------
+        // On an abort (a wait gave up) the group keeps running the same loops
+        // and named barriers -- so no thread can be left waiting at one -- but
+        // stops reading TMEM; the fault word already records the failure.
+        const int q4 = warp & 3;             // TMEM lane quadrant of this warp
+        const int row = q4 * 32 + lane;      // token of S^T, dim of O^T
+        const int wt = tid - 64;             // 0..127 within the group
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        auto group_sync = [] { named_barrier(1, 128); };
+        uint32_t j = 0;
+        bool aborted = false;
+        for (int64_t t = my_start; t < my_end;) {
+            const Piece P = piece_at(t, my_end, prefix, a);
+            const bool first_piece = t == my_start;
+            t += P.k1 - P.k0;
+            const int L = __ldg(a.seq_lens + P.b);
+            float m_run[G], l_part[G], acc[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                m_run[h] = -INFINITY;
+                l_part[h] = 0.f;
+                acc[h] = 0.f;
+            }
+            for (int k = P.k0; k < P.k1; ++k, ++j) {
+                const uint32_t buf = j & 1, par = (j >> 1) & 1;
+                aborted = aborted || !mbar_wait(&s_full[buf], par, abort_flag, fault);
+                float s[GN];
+#pragma unroll
+                for (int i = 0; i < GN; ++i) s[i] = 0.f;
+                if (!aborted) {
+                    tc_fence_after();
+                    tmem_ld_32x32b<GN>(tmem + buf * 16 + lane_off, s);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                }
+                mbar_arrive(&s_empty[buf]);
+                const int valid = min(kTcTile, L - k * kTcTile);
+                const bool live = row < valid;
+                float x[G];
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    x[h] = live ? s[h] * a.scale_log2 : -INFINITY;
+                    const float wm = warp_max(x[h]);
+                    if (lane == 0) red[buf * 64 + q4 * 16 + h] = wm;
+                }
+                group_sync();
+                float alpha[G];
+                unsigned char *pbuf = sm + kTcPOff + buf * kTcPBuf;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float *rr = red + buf * 64 + h;
+                    const float tmax = fmaxf(fmaxf(rr[0], rr[16]), fmaxf(rr[32], rr[48]));
+                    const float m_new = fmaxf(m_run[h], tmax);
+                    alpha[h] = exp2f(m_run[h] - m_new);
+                    m_run[h] = m_new;
+                    const float p = exp2f(x[h] - m_new);
+                    const T hi = from_f32<T>(p);
+                    const T lo = from_f32<T>(p - static_cast<float>(hi));
+                    l_part[h] = l_part[h] * alpha[h] + p;
+                    *reinterpret_cast<T *>(pbuf + sw128_offset(h, row, kPChunk)) = hi;
+                    *reinterpret_cast<T *>(pbuf + sw128_offset(LO + h, row, kPChunk)) = lo;
+                }
+                if (!live) {  // V rows past the length may hold anything: zero them
+                    unsigned char *vrow =
+                        sm + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf + row * 128;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        reinterpret_cast<uint4 *>(vrow)[i] = make_uint4(0, 0, 0, 0);
+                        reinterpret_cast<uint4 *>(vrow + kTcHalf)[i] = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&p_full[buf]);
+                aborted = aborted || !mbar_wait(&o_full[buf], par, abort_flag, fault);
+                float o[PN];
+#pragma unroll
+                for (int i = 0; i < PN; ++i) o[i] = 0.f;
+                if (!aborted) {
+                    tc_fence_after();
+                    tmem_ld_32x32b<PN>(tmem + 32 + buf * PN + lane_off, o);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                }
+                mbar_arrive(&o_empty[buf]);
+#pragma unroll
+                for (int h = 0; h < G; ++h) acc[h] = acc[h] * alpha[h] + (o[h] + o[LO + h]);
+            }
+            // ---- finish the piece: l over the group, then output or partial ----
+            float l[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float ls = warp_sum(l_part[h]);
+                if (lane == 0) lred[q4 * 16 + h] = ls;
+            }
+            group_sync();
+#pragma unroll
+            for (int h = 0; h < G; ++h) l[h] = lred[h] + lred[16 + h] + lred[32 + h] + lred[48 + h];
+            group_sync();
+            OT *out = static_cast<OT *>(a.out) + ((int64_t)P.b * q_heads + (int64_t)P.g * G) * 128;
+            if (P.k0 == 0 && P.k1 == P.nt) {  // the whole segment ran here
+#pragma unroll
+                for (int h = 0; h < G; ++h)
+                    out[h * 128 + row] = from_f32<OT>(l[h] > 0.f ? acc[h] / l[h] : 0.f);
+                continue;
+            }
+            const int kslot = first_piece ? 0 : 1;
+            const int64_t slot = ((int64_t)blockIdx.x * 2 + kslot) * 16;
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                a.part_o[(slot + h) * 128 + row] = acc[h];
+                if (wt == h) {
+                    a.part_ml[(slot + h) * 2] = m_run[h];
+                    a.part_ml[(slot + h) * 2 + 1] = l[h];
+                }
+            }
+            if (!a.merge_in_kernel) continue;
+            const int np = cta_of_tile(P.seg + P.nt - 1, ncta, total_tiles) -
+                           cta_of_tile(P.seg, ncta, total_tiles) + 1;
+            group_sync();
+            if (wt == 0) {
+                __threadfence();  // publishes the group's partials (bar.sync is cumulative)
+                const uint32_t tk = atomicAdd(a.counters + (int64_t)P.b * a.kv_heads + P.g, 1u);
+                *ticket = tk == (uint32_t)(np - 1);
+            }
+            group_sync();
+            if (*ticket) {
+                __threadfence();
+#pragma unroll 1
+                for (int h = 0; h < G; ++h)
+                    merge_head<OT>(a, h, P.seg, P.nt, ncta, total_tiles, wt, 128, mstage,
+                                   kInKernelMergeMax, out + h * 128, group_sync);
+                if (wt == 0) a.counters[(int64_t)P.b * a.kv_heads + P.g] = 0u;
+            }
+        }
+        // empty sequences: no tile, zero output (the SDK's all-masked rule)
+        for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
+            if (__ldg(a.seq_lens + b) > 0) continue;
+            OT *ob = static_cast<OT *>(a.out) + (int64_t)b * q_heads * 128;
+            for (int h = 0; h < q_heads; ++h) ob[h * 128 + row] = from_f32<OT>(0.f);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTcTmemCols);
+}
+
+// Merges segments that span more than kInKernelMergeMax CTAs.  Grid:
+// (kv_heads * G, batch); block: 128 threads, one output element each.
+template <typename OT>
+__global__ void __launch_bounds__(128)
+pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
+    __shared__ float stage[3 * kTcMaxGrid];
+    const int b = blockIdx.y;
+    const int g = blockIdx.x / group, h = blockIdx.x - g * group;
+    const int64_t T = a.tile_prefix[a.batch];
+    const int ncta = (int)min((int64_t)grid, max(T, (int64_t)1));  // as the decode kernel
+    const int nt = (a.tile_prefix[b + 1] - a.tile_prefix[b]) / a.kv_heads;
+    if (nt == 0 || T == 0) return;
+    const int64_t seg = a.tile_prefix[b] + (int64_t)g * nt;
+    if (cta_of_tile(seg, ncta, T) == cta_of_tile(seg + nt - 1, ncta, T)) return;
+    OT *out = static_cast<OT *>(a.out) +
+              ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) * 128;
+    merge_head<OT>(a, h, seg, nt, ncta, T, threadIdx.x, 128, stage, kTcMaxGrid, out,
+                   [] { __syncthreads(); });
+}
+
 int g_sm_count[64];
 
 int sm_count() {
@@ -415,7 +987,6 @@ int sm_count() {
     return g_sm_count[dev];
 }
 
-size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
 struct WsLayout {
     size_t counters, ml, o, total;
@@ -431,14 +1002,17 @@ WsLayout ws_layout(size_t batch, size_t q_heads, size_t kv_heads, size_t head_di
     return w;
 }
 
-size_t pick_chunk(size_t chunk_tokens) {
-    size_t c = chunk_tokens == 0 ? 256 : chunk_tokens;
-    return round_up(c, kTile);
+// Positions per work unit: a multiple of the 128-token tcgen05 tile.  0
+// picks from the longest sequence (bigger splits for long contexts).
+size_t pick_chunk(size_t chunk_tokens, size_t max_seq_len) {
+    size_t c = chunk_tokens;
+    if (c == 0) c = max_seq_len <= 4096 ? 256 : (max_seq_len <= 32768 ? 512 : 1024);
+    return round_up(c, 128);
 }
 
 template <int HD, int G, typename T, typename OT>
 int launch_decode(const DecodeArgs &args, cudaStream_t stream) {
-    auto kern = paged_decode_kernel<HD, G, T, OT>;
+    auto kern = paged_decode_simt_kernel<HD, G, T, OT>;
     const size_t smem = smem_bytes<HD, G>(args.batch);
     static int configured[64];
     int dev = 0;
@@ -461,6 +1035,89 @@ int dispatch_out(const DecodeArgs &args, PkvDType out, cudaStream_t s) {
     return launch_decode<HD, G, T, __nv_bfloat16>(args, s);
 }
 
+// ---- tcgen05 path host side ----
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D view of one pool: [rows][kv_width] two-byte elements, box = one page
+// of one 64-column half, 128-byte swizzle (the UMMA canonical layout).
+bool encode_pool_map(CUtensorMap *map, const void *pool, uint64_t rows, uint64_t kv_width,
+                     uint32_t block_size, bool bf16) {
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    cuuint64_t dims[2] = {kv_width, rows};
+    cuuint64_t strides[1] = {kv_width * 2};
+    cuuint32_t box[2] = {64, block_size};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+               const_cast<void *>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int G, typename T, typename OT>
+int launch_tc(const TcArgs &args, const CUtensorMap &km, const CUtensorMap &vm, int ncta,
+              cudaStream_t stream) {
+    auto kern = paged_decode_tc_kernel<G, T, OT>;
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)tc_smem_bytes(kTcMaxBatch)) != cudaSuccess)
+            return 0;
+        configured[dev] = 1;
+    }
+    kern<<<ncta, kTcThreads, tc_smem_bytes(args.batch), stream>>>(args, km, vm);
+    if (!args.merge_in_kernel)
+        pkv_tc_merge_kernel<OT><<<dim3(args.kv_heads * G, args.batch), 128, 0, stream>>>(args, G,
+                                                                                         ncta);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+template <typename T, typename OT>
+int dispatch_tc_group(const TcArgs &args, int group, const CUtensorMap &km, const CUtensorMap &vm,
+                      int ncta, cudaStream_t s) {
+    switch (group) {
+        case 1: return launch_tc<1, T, OT>(args, km, vm, ncta, s);
+        case 2: return launch_tc<2, T, OT>(args, km, vm, ncta, s);
+        case 4: return launch_tc<4, T, OT>(args, km, vm, ncta, s);
+        case 8: return launch_tc<8, T, OT>(args, km, vm, ncta, s);
+        case 16: return launch_tc<16, T, OT>(args, km, vm, ncta, s);
+        default: return 0;
+    }
+}
+
+int dispatch_tc(const TcArgs &args, int group, bool bf16, PkvDType out, const CUtensorMap &km,
+                const CUtensorMap &vm, int ncta, cudaStream_t s) {
+    if (!bf16)
+        return out == PKV_DTYPE_F32
+                   ? dispatch_tc_group<__half, float>(args, group, km, vm, ncta, s)
+                   : dispatch_tc_group<__half, __half>(args, group, km, vm, ncta, s);
+    return out == PKV_DTYPE_F32
+               ? dispatch_tc_group<__nv_bfloat16, float>(args, group, km, vm, ncta, s)
+               : dispatch_tc_group<__nv_bfloat16, __nv_bfloat16>(args, group, km, vm, ncta, s);
+}
+
+bool tc_eligible(size_t head_dim, size_t block_size, size_t group, size_t rows) {
+    const char *force = getenv("PKV_DECODE_KERNEL");
+    if (force != nullptr && strcmp(force, "simt") == 0) return false;
+    return head_dim == 128 && (block_size == 16 || block_size == 32 || block_size == 64 ||
+                               block_size == 128) &&
+           (group == 1 || group == 2 || group == 4 || group == 8 || group == 16) &&
+           rows < (size_t(1) << 31);
+}
+
 template <int HD, typename T>
 int dispatch_group(const DecodeArgs &args, int group, PkvDType out, cudaStream_t s) {
     switch (group) {
@@ -479,10 +1136,13 @@ extern "C" {
 
 size_t pkv_decode_workspace_bytes(size_t batch, size_t q_heads, size_t head_dim,
                                   size_t max_seq_len, size_t chunk_tokens) {
-    const size_t chunk = pkv::pick_chunk(chunk_tokens);
+    const size_t chunk = pkv::pick_chunk(chunk_tokens, max_seq_len);
     const size_t max_chunks = max_seq_len / chunk + 1;
-    // kv_heads only sizes the ticket counters; q_heads bounds it.
-    return pkv::ws_layout(batch, q_heads, q_heads, head_dim, max_chunks).total;
+    // kv_heads only sizes the ticket counters; q_heads bounds it.  The larger
+    // of the two kernels' layouts, so either may run.
+    const size_t simt = pkv::ws_layout(batch, q_heads, q_heads, head_dim, max_chunks).total;
+    const size_t tc = pkv::tc_workspace(batch, q_heads).total;
+    return simt > tc ? simt : tc;
 }
 
 int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes, PkvStream stream,
@@ -530,9 +1190,13 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         return 0;
     }
     const size_t group = q_heads / kvh;
-    if (group != 1 && group != 2 && group != 4 && group != 8) {
+    const bool use_tc = pkv::tc_eligible(hd, layer->block_size, group,
+                                         layer->block_count * layer->block_size);
+    if (group != 1 && group != 2 && group != 4 && group != 8 && !(use_tc && group == 16)) {
         pkv_internal_set_error(error, error_capacity,
-                               "%s: q_heads/kv_heads must be 1, 2, 4 or 8 (got %zu)", what, group);
+                               "%s: q_heads/kv_heads must be 1, 2, 4 or 8 (16 with head_dim 128 "
+                               "and pages of 16-128 tokens), got %zu",
+                               what, group);
         return 0;
     }
     if (batch->batch == 0 || batch->batch > (size_t)pkv::kMaxBatch || batch->table_stride == 0 ||
@@ -548,13 +1212,15 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         pkv_internal_set_error(error, error_capacity, "%s: buffers must be 16-byte aligned", what);
         return 0;
     }
-    const size_t chunk = pkv::pick_chunk(chunk_tokens);
+    const size_t chunk = pkv::pick_chunk(chunk_tokens, max_seq_len);
     const size_t max_chunks = max_seq_len / chunk + 1;
     const pkv::WsLayout ws = pkv::ws_layout(batch->batch, q_heads, kvh, hd, max_chunks);
-    if (workspace == nullptr || workspace_bytes < ws.total || ((uintptr_t)workspace % 256) != 0) {
+    const pkv::TcWorkspace tws = pkv::tc_workspace(batch->batch, kvh);
+    const size_t need = use_tc ? tws.total : ws.total;
+    if (workspace == nullptr || workspace_bytes < need || ((uintptr_t)workspace % 256) != 0) {
         pkv_internal_set_error(error, error_capacity,
                                "%s: workspace needs %zu bytes, 256-byte aligned (got %zu)", what,
-                               ws.total, workspace_bytes);
+                               need, workspace_bytes);
         return 0;
     }
     pkv::DecodeArgs a;
@@ -585,7 +1251,47 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
     a.scale_log2 = scale * pkv::kLog2e;
     const cudaStream_t s = (cudaStream_t)stream;
     int ok;
-    if (layer->dtype == PKV_DTYPE_F16)
+    if (use_tc) {
+        CUtensorMap km, vm;
+        const bool bf16 = layer->dtype == PKV_DTYPE_BF16;
+        const uint64_t rows = (uint64_t)layer->block_count * layer->block_size;
+        if (!pkv::encode_pool_map(&km, layer->key_pool, rows, kvh * hd, (uint32_t)layer->block_size,
+                                  bf16) ||
+            !pkv::encode_pool_map(&vm, layer->value_pool, rows, kvh * hd,
+                                  (uint32_t)layer->block_size, bf16)) {
+            pkv_internal_set_error(error, error_capacity, "%s: tensor map encoding failed", what);
+            return 0;
+        }
+        const int ncta = pkv::sm_count() < pkv::kTcMaxGrid ? pkv::sm_count() : pkv::kTcMaxGrid;
+        auto *wsb = static_cast<unsigned char *>(workspace);
+        pkv::TcArgs t;
+        t.counters = reinterpret_cast<uint32_t *>(wsb + tws.counters);
+        t.part_ml = reinterpret_cast<float *>(wsb + tws.ml);
+        t.part_o = reinterpret_cast<float *>(wsb + tws.o);
+        t.tile_prefix = reinterpret_cast<int32_t *>(wsb + tws.prefix);
+        t.table_stride = (int32_t)batch->table_stride;
+        t.kv_heads = (int32_t)kvh;
+        t.block_size = (int32_t)layer->block_size;
+        t.block_count = (uint32_t)layer->block_count;
+        t.scale_log2 = scale * pkv::kLog2e;
+        t.merge_in_kernel = ncta / (int)kvh + 2 <= pkv::kInKernelMergeMax;
+        // launches of at most kTcMaxBatch sequences (their prefix lives in smem)
+        const size_t osz = output_dtype == PKV_DTYPE_F32 ? 4 : 2;
+        ok = 1;
+        for (size_t b0 = 0; ok && b0 < batch->batch; b0 += pkv::kTcMaxBatch) {
+            const size_t n = batch->batch - b0 < (size_t)pkv::kTcMaxBatch
+                                 ? batch->batch - b0
+                                 : (size_t)pkv::kTcMaxBatch;
+            pkv::TcArgs sl = t;
+            sl.batch = (int32_t)n;
+            sl.tables = batch->block_tables + b0 * batch->table_stride;
+            sl.seq_lens = batch->seq_lens + b0;
+            sl.query = static_cast<const char *>(query) + b0 * q_heads * hd * 2;
+            sl.out = static_cast<char *>(output) + b0 * q_heads * hd * osz;
+            sl.counters = t.counters + b0 * kvh;
+            ok = pkv::dispatch_tc(sl, (int)group, bf16, output_dtype, km, vm, ncta, s);
+        }
+    } else if (layer->dtype == PKV_DTYPE_F16)
         ok = hd == 128 ? pkv::dispatch_group<128, __half>(a, (int)group, output_dtype, s)
                        : pkv::dispatch_group<64, __half>(a, (int)group, output_dtype, s);
     else

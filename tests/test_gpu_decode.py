@@ -33,6 +33,12 @@ def _run_decode(case: PagedCase, out_dtype=None, chunk: int = 0, max_len: int | 
     return out.float().cpu().numpy(), ws
 
 
+def _round_like(x: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    return W.bf16_bits_to_f32(W.f32_to_bf16_bits(x))
+
+
 def _oracle(case: PagedCase, oracle_mod):
     return oracle_mod.paged_decode(case.q, case.dtype, case.kpool, case.vpool, case.kv_heads,
                                    case.head_dim, case.block_size, case.tables, case.lengths,
@@ -69,10 +75,63 @@ def test_decode_matches_oracle(lib, oracle_mod, cuda, group, head_dim, dtype):
     case = PagedCase(lengths, kvh * group, kvh, head_dim, 16, dtype, seed=group * 100 + head_dim,
                      device=cuda)
     want = _oracle(case, oracle_mod)
-    for out_dtype, chunk in [(torch.float32, 0), (torch.float32, 64), (case.d_q.dtype, 128)]:
-        got, _ = _run_decode(case, out_dtype, chunk)
+    for chunk in (0, 64, 128):
+        got, _ = _run_decode(case, torch.float32, chunk)
         check_close(got, want, f"group {group} d {head_dim} {dtype} chunk {chunk}")
+        # a storage-dtype output is the same FP32 result rounded to nearest even
+        half, _ = _run_decode(case, case.d_q.dtype, chunk)
+        assert np.array_equal(half, _round_like(got, dtype)), f"{dtype} output rounding"
     assert P.device_fault(0) == 0
+
+
+@pytest.mark.parametrize("group,block_size,dtype", [
+    (16, 16, "f16"), (4, 32, "bf16"), (8, 64, "f16"), (2, 128, "f16")])
+def test_tcgen05_shapes(lib, oracle_mod, cuda, group, block_size, dtype):
+    """GQA 16 and page sizes 32..128 (tcgen05 path only, head_dim 128)."""
+    import torch
+    lengths = [1, 127, 128, 129, 300, 1000]
+    case = PagedCase(lengths, 2 * group, 2, 128, block_size, dtype, seed=group + block_size,
+                     device=cuda)
+    want = _oracle(case, oracle_mod)
+    for chunk in (0, 128, 256):
+        got, _ = _run_decode(case, torch.float32, chunk)
+        check_close(got, want, f"group {group} block {block_size} chunk {chunk}")
+    assert P.device_fault(0) == 0
+
+
+def test_wide_split_uses_merge_kernel(lib, oracle_mod, cuda):
+    """One KV head and one long sequence: every CTA takes a piece of the same
+    (sequence, head) segment, so the separate merge kernel combines ~148
+    partials (config 4's per-GPU shape after the head split)."""
+    import torch
+    case = PagedCase([40000, 3], 8, 1, 128, 16, "f16", seed=21, device=cuda)
+    want = _oracle(case, oracle_mod)
+    got, _ = _run_decode(case, torch.float32)
+    check_close(got, want, "wide split")
+    assert P.device_fault(0) == 0
+
+
+def test_batch_above_one_launch(lib, oracle_mod, cuda):
+    """More sequences than one tcgen05 launch holds (1024): sliced launches."""
+    import torch
+    lengths = (W.uniform(5, 1100) * 300).astype(np.int64)
+    case = PagedCase(lengths, 4, 1, 128, 16, "f16", seed=22, device=cuda)
+    want = _oracle(case, oracle_mod)
+    got, _ = _run_decode(case, torch.float32)
+    check_close(got, want, "1100 sequences")
+
+
+@pytest.mark.parametrize("group", [1, 4, 8])
+def test_simt_kernel_head_dim_128(lib, oracle_mod, cuda, monkeypatch, group):
+    """The CUDA-core kernel (forced) on the shapes the tcgen05 kernel serves."""
+    import torch
+    monkeypatch.setenv("PKV_DECODE_KERNEL", "simt")
+    lengths = [0, 1, 16, 17, 200, 777]
+    case = PagedCase(lengths, 2 * group, 2, 128, 16, "f16", seed=50 + group, device=cuda)
+    want = _oracle(case, oracle_mod)
+    for chunk in (0, 128):
+        got, _ = _run_decode(case, torch.float32, chunk)
+        check_close(got, want, f"simt group {group} chunk {chunk}")
 
 
 def test_decode_ignores_poison_past_length(lib, oracle_mod, cuda):

@@ -68,8 +68,8 @@ def test_prefix_import_then_decode_steps(lib, oracle_mod, cuda):
     kv = kvh * d
     host_k = [W.normal_bits(40 + l, (sum(past), kv), "f16", stream=1) for l in range(layers)]
     host_v = [W.normal_bits(40 + l, (sum(past), kv), "f16", stream=2) for l in range(layers)]
-    # prefix import: current length 0, past given, every token new
-    pool.step_begin(seqs, past, past_lengths=past)
+    # prefix import: every token of the prefix is new in this step
+    pool.step_begin(seqs, past)
     for l in range(layers):
         P.kv_import(pool.layer(l), pool.step_batch(), to_device_bits(host_k[l], "f16", cuda),
                     to_device_bits(host_v[l], "f16", cuda), pool.step_row_offsets())
@@ -124,7 +124,7 @@ def test_step_rollback_and_atomic_failure(lib, cuda):
     free0 = cache.free_blocks()
     # explicit rollback: lengths and pages come back, locks are released
     pool.step_begin(seqs, [20, 1, 17])
-    assert cache.free_blocks() == free0 - 3
+    assert cache.free_blocks() == free0 - 5  # 36, 17, 33 tokens: 2 + 1 + 2 pages
     pool.step_end(False)
     assert cache.free_blocks() == free0 and [cache.length(s) for s in seqs] == [16, 16, 16]
     assert all(cache.begin_decode(s) for s in seqs)
