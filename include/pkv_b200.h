@@ -131,6 +131,23 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch,
                      size_t workspace_bytes, PkvStream stream, char *error,
                      size_t error_capacity);
 
+/* Paged decode that allocates nothing: pkv_paged_decode with its scratch in
+ * a static 8 MiB device array inside this library instead of a workspace.
+ * No counterpart in the SDK.  For callers that cannot allocate device memory
+ * at call time (a serving loop whose device memory is planned once up front,
+ * where cudaMalloc could synchronise the device or fragment the pool; a host
+ * behind an FFI that only passes the buffers it was given).  Shapes whose
+ * scratch would exceed 8 MiB fail with an error naming the size.  Every GPU
+ * that loads the library holds the 8 MiB until exit.  The first call on a
+ * device looks up the array's device address (once per device), so make it
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU (other streams, other threads) race; serialise them. */
+int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const PkvBatch *batch,
+                                    size_t q_heads, const void *query, float scale,
+                                    void *output, PkvDType output_dtype,
+                                    size_t max_seq_len, PkvStream stream, char *error,
+                                    size_t error_capacity);
+
 /* Chunked prefill over the paged cache (tcgen05 tensor cores, FP32
  * accumulation in TMEM).  Sequence b contributes query rows
  * query_offsets[b] .. query_offsets[b+1]-1 ([total_q][q_heads][head_dim]);

@@ -82,6 +82,8 @@ EXPORTS = {
     "pkv_decode_workspace_init": (_c_int, [_c_ptr, _c_size, _c_ptr, *_ERR]),
     "pkv_paged_decode": (_c_int, [_LP, _BP, _c_size, _c_ptr, ctypes.c_float, _c_ptr, _c_int,
                                   _c_size, _c_size, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_paged_decode_static_scratch": (_c_int, [_LP, _BP, _c_size, _c_ptr, ctypes.c_float,
+                                                 _c_ptr, _c_int, _c_size, _c_ptr, *_ERR]),
     "pkv_paged_prefill": (_c_int, [_LP, _BP, _c_size, _c_ptr, _c_ptr, _c_size, _c_size,
                                    ctypes.c_float, _c_int, _c_ptr, _c_int, _c_ptr, *_ERR]),
     "pkv_device_fault": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_uint32), *_ERR]),
@@ -285,6 +287,15 @@ def paged_decode(layer: PkvPagedLayer, batch: PkvBatch, query, output, scale: fl
     _call("pkv_paged_decode", ctypes.byref(layer), ctypes.byref(batch), q_heads,
           query.data_ptr(), ctypes.c_float(scale), output.data_ptr(), _dtype_code(output),
           max_seq_len, chunk_tokens, workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+
+
+def paged_decode_static_scratch(layer: PkvPagedLayer, batch: PkvBatch, query, output,
+                                scale: float, max_seq_len: int, stream=None) -> None:
+    """pkv_paged_decode with the library's static device scratch (no workspace)."""
+    q_heads = query.shape[-2]
+    _call("pkv_paged_decode_static_scratch", ctypes.byref(layer), ctypes.byref(batch), q_heads,
+          query.data_ptr(), ctypes.c_float(scale), output.data_ptr(), _dtype_code(output),
+          max_seq_len, _stream_ptr(stream))
 
 
 def paged_prefill(layer: PkvPagedLayer, batch: PkvBatch, query, query_offsets, output,

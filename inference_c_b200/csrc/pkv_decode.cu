@@ -25,6 +25,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
 #include "pkv_sm100.cuh"
@@ -1312,3 +1314,93 @@ int pkv_internal_take_decode_fault(uint32_t *code) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without caller-provided scratch.
+//
+// For callers that cannot allocate device memory when they call decode --
+// for instance a serving loop whose device memory is planned once up front
+// (cudaMalloc may synchronise the device and fragments a pre-sized pool), or
+// a host bound through an FFI that only passes the buffers it was handed and
+// has no way to own extra device memory.  The split-K scratch lives in the
+// static device array below instead: every GPU that loads this library holds
+// kDecodeStaticScratchBytes (8 MiB) of it until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kDecodeStaticScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_decode_static_scratch[kDecodeStaticScratchBytes];
+
+std::mutex g_static_scratch_lock;
+void *g_static_scratch_addr[64];  // device address of the array, per device
+
+// The array's device address for the current device, looked up once per
+// device (with that device current).  In host code the symbol itself is only
+// a host-side stand-in and must never be handed to a kernel.
+void *static_scratch_for_current_device(char *error, size_t cap) {
+    int dev = -1;
+    cudaError_t st = cudaGetDevice(&dev);
+    if (st != cudaSuccess || dev < 0 || dev >= 64) {
+        pkv_internal_set_error(error, cap, "pkv_paged_decode_static_scratch: no usable device (%s)",
+                               cudaGetErrorString(st));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> guard(g_static_scratch_lock);
+    if (g_static_scratch_addr[dev] == nullptr) {
+        void *p = nullptr;
+        st = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+        if (st != cudaSuccess || p == nullptr) {
+            pkv_internal_set_error(error, cap,
+                                   "pkv_paged_decode_static_scratch: cudaGetSymbolAddress failed: %s",
+                                   cudaGetErrorString(st));
+            return nullptr;
+        }
+        g_static_scratch_addr[dev] = p;
+    }
+    return g_static_scratch_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const PkvBatch *batch,
+                                               size_t q_heads, const void *query, float scale,
+                                               void *output, PkvDType output_dtype,
+                                               size_t max_seq_len, PkvStream stream, char *error,
+                                               size_t error_capacity) {
+    const char *what = "pkv_paged_decode_static_scratch";
+    if (layer == nullptr || batch == nullptr || layer->kv_heads == 0) {
+        pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    // Scratch of the kernel pkv_paged_decode will pick for this shape;
+    // anything above the array is refused.
+    const size_t kvh = layer->kv_heads, hd = layer->head_dim;
+    const size_t group = q_heads % kvh == 0 ? q_heads / kvh : 0;
+    size_t need;
+    if (pkv::tc_eligible(hd, layer->block_size, group, layer->block_count * layer->block_size)) {
+        need = pkv::tc_workspace(batch->batch, kvh).total;
+    } else {
+        const size_t chunk = pkv::pick_chunk(0, max_seq_len);
+        need = pkv::ws_layout(batch->batch, q_heads, kvh, hd, max_seq_len / chunk + 1).total;
+    }
+    if (need > kDecodeStaticScratchBytes) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: this shape needs %zu bytes of scratch, above the static "
+                               "maximum of %zu bytes; use pkv_paged_decode with a workspace",
+                               what, need, kDecodeStaticScratchBytes);
+        return 0;
+    }
+    void *scratch = static_scratch_for_current_device(error, error_capacity);
+    if (scratch == nullptr) return 0;
+    // The split-K tickets must start at zero; both layouts keep them first.
+    const size_t tickets = pkv::round_up(batch->batch * layer->kv_heads * sizeof(uint32_t), 256);
+    const cudaError_t st = cudaMemsetAsync(scratch, 0, tickets, (cudaStream_t)stream);
+    if (st != cudaSuccess) {
+        pkv_internal_set_error(error, error_capacity, "%s: clearing the tickets failed: %s", what,
+                               cudaGetErrorString(st));
+        return 0;
+    }
+    return pkv_paged_decode(layer, batch, q_heads, query, scale, output, output_dtype,
+                            max_seq_len, 0, scratch, kDecodeStaticScratchBytes, stream, error,
+                            error_capacity);
+}
