@@ -70,6 +70,19 @@ def peak_hbm() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def traffic_ratio(cfg: int):
+    """DRAM bytes per algorithmic byte of the decode kernel, from the ncu
+    capture summarised in profiles/decode_tc_cfg<cfg>.md (None if absent)."""
+    f = ROOT / "profiles" / f"decode_tc_cfg{cfg}.md"
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 def metric_name(cfg: int) -> str:
     return ("paged decode attention tokens/s (config %d: append 1 token per sequence + paged "
             "SDPA per step)" % cfg)
@@ -427,6 +440,7 @@ def run_ours(args) -> None:
     alg_bytes = statistics.mean(bytes_log)
     peak, peak_kind = peak_hbm()
     achieved = alg_bytes / (mean_dec / 1e3) / 1e9
+    ratio = traffic_ratio(cfg)
     per_rank = {"rank": rank, "decode_ms": mean_dec, "gbs": achieved, "seqs": n,
                 "tokens": int(cur.sum())}
     gathered = [per_rank]
@@ -454,7 +468,11 @@ def run_ours(args) -> None:
             "data": "synthetic: seeded N(0,1) FP16 Q/K/V on the device, seeded lengths",
             "config": config_block(cfg, world, chunk),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": None if ratio is None else ratio * alg_bytes,
+                         "traffic_source": (f"ncu dram__bytes_read+write of one launch, as a ratio "
+                                            f"to algorithmic bytes ({ratio}), "
+                                            f"profiles/decode_tc_cfg{cfg}.md"),
                          "peak_kind": peak_kind, "kernel": "paged_decode_kernel",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "mean_launch_ms": mean_dec, "per_rank": gathered},
