@@ -1,10 +1,537 @@
 // pkv_prefill.cu -- chunked prefill attention over the paged cache (sm_100a).
+//
+// Each sequence b brings n_b new query rows that are its last n_b positions
+// (the chunk just appended); with `causal` query j attends to keys
+// 0 .. L_b - n_b + j, the SDK's causal offset kv_len - q_len
+// (attention.c:251, :352-353), otherwise to all L_b keys.
+//
+// Work item = (sequence, query head, tile of 128 query rows).  One persistent
+// 192-thread CTA per SM, warp-specialised:
+//   warp 0     producer: TMA-loads the item's 128 query rows (a 3-D box over
+//              [rows][heads][128]) and, per 128-key tile, every page of K and
+//              V for the item's KV head straight from the pool (2-D boxes of
+//              one page x 64 columns); K ring of 3 and V ring of 2 stages;
+//   warp 1     one thread issues tcgen05.mma:
+//                S[128 q][128 k]  = Q[128][128] . K^T            (smem x smem)
+//                O[128 q][128 d] += P[128 q][128 k] . V[128 k][128] (P from TMEM)
+//   warps 2-5  softmax: thread r owns query row r (TMEM lane r), so the row
+//              max and sum need no cross-thread reduction.  P goes back to
+//              TMEM as packed 16-bit pairs and feeds the PV MMA directly.
+// O accumulates in TMEM (FP32).  The running max is only raised when a tile's
+// max exceeds it by more than 2^8 (lazy rescale: O is rescaled in TMEM only
+// on those tiles).  P is written as a 16-bit high half and a low half
+// (p - round(p)), and a second PV MMA adds the low half: with P rounded to
+// bf16 alone the output error (~1e-4 absolute at 2k-10k keys) stays inside
+// max-abs 2e-3 but its tail breaks max-rel 1e-2 on outputs near 1e-2, so the
+// split is kept for every context length (kPreciseKeys above any length).
+// S is double-buffered so the QK^T MMA of tile j+1 overlaps the softmax of
+// tile j.  TMEM columns: S 2 x 128, O 128, P 64, P-low 64 = 512.
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <stdio.h>
+
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_sm100.cuh"
 
 namespace pkv {
 namespace {
+
 __device__ uint32_t g_prefill_fault;
+
+constexpr int kPfThreads = 192;
+constexpr int kPfTile = 128;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+constexpr int kPfMaxBatch = 512;
+constexpr int kPreciseKeys = 1 << 30;  // hi/lo P for every length (see above)
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+constexpr uint32_t kHalf = 16384;         // 128 rows x 128 bytes
+constexpr uint32_t kQOff = 0;             // Q [2 halves][128][64]
+constexpr uint32_t kKOff = 32768;         // K stages of 32 KiB
+constexpr uint32_t kVOff = kKOff + kKStages * 32768;
+constexpr uint32_t kBarOff = kVOff + kVStages * 32768;
+constexpr uint32_t kMiscOff = kBarOff + 256;
+constexpr uint32_t kPrefixOff = kMiscOff + 256;
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384, kColPlo = 448, kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+size_t pf_smem_bytes(int batch) { return kPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
+
+struct PfArgs {
+    const uint32_t *tables;
+    const int32_t *seq_lens;
+    const int32_t *q_offsets;
+    void *out;
+    int32_t table_stride;
+    int32_t batch;
+    int32_t q_heads;
+    int32_t kv_heads;
+    int32_t block_size;
+    uint32_t block_count;
+    float scale_log2;
+    int32_t causal;
+};
+
+struct Item {
+    int b, h, g, q0, nrows, L, pos0, ntiles;
+    bool precise, bad;
+};
+
+__device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfArgs &a) {
+    Item I;
+    int lo = 0, hi = a.batch - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    I.b = lo;
+    const int qstart = __ldg(a.q_offsets + lo);
+    const int nq = __ldg(a.q_offsets + lo + 1) - qstart;
+    const int nqt = (nq + kPfTile - 1) / kPfTile;
+    const int w = (int)(u - prefix[lo]);
+    const int qt = nqt - 1 - w / a.q_heads;  // longest tiles of a sequence first
+    I.h = w - (w / a.q_heads) * a.q_heads;
+    I.g = I.h / (a.q_heads / a.kv_heads);
+    I.q0 = qstart + qt * kPfTile;
+    I.nrows = min(kPfTile, nq - qt * kPfTile);
+    I.L = __ldg(a.seq_lens + lo);
+    I.bad = nq > I.L;
+    I.pos0 = I.L - nq + qt * kPfTile;
+    const int kmax = a.causal ? min(I.L, I.pos0 + I.nrows) : I.L;
+    I.ntiles = I.bad ? 0 : (kmax + kPfTile - 1) / kPfTile;
+    I.precise = kmax < kPreciseKeys;
+    return I;
+}
+
+__device__ void build_item_prefix(const PfArgs &a, int *prefix, int *scratch) {
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (a.batch + nthr - 1) / nthr;
+    int local = 0;
+    for (int k = 0; k < per; ++k) {
+        const int b = tid * per + k;
+        if (b < a.batch) {
+            const int nq = __ldg(a.q_offsets + b + 1) - __ldg(a.q_offsets + b);
+            local += (max(nq, 0) + kPfTile - 1) / kPfTile * a.q_heads;
+        }
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += scratch[w];
+    int run = before + incl - local;
+    for (int k = 0; k < per; ++k) {
+        const int b = tid * per + k;
+        if (b < a.batch) {
+            prefix[b] = run;
+            const int nq = __ldg(a.q_offsets + b + 1) - __ldg(a.q_offsets + b);
+            run += (max(nq, 0) + kPfTile - 1) / kPfTile * a.q_heads;
+        }
+    }
+    if (tid == nthr - 1) prefix[a.batch] = before + incl;
+}
+
+template <typename T>
+struct Bf16Flag { static constexpr bool value = false; };
+template <>
+struct Bf16Flag<__nv_bfloat16> { static constexpr bool value = true; };
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+    return __half22float2(*reinterpret_cast<__half2 *>(&v));
+}
+
+template <typename T, typename OT>
+__global__ void __launch_bounds__(kPfThreads, 1)
+paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap,
+                        const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap) {
+    using namespace sm100;
+    constexpr uint32_t kIdescS = idesc_f16(128, 128, Bf16Flag<T>::value, false, false);
+    constexpr uint32_t kIdescPV = idesc_f16(128, 128, Bf16Flag<T>::value, false, true);
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *sm = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kBarOff);
+    uint64_t *kfull = bars, *kempty = bars + 3, *vfull = bars + 6, *vempty = bars + 8;
+    uint64_t *s_full = bars + 10, *s_empty = bars + 12, *p_full = bars + 14, *o_full = bars + 15;
+    uint64_t *q_full = bars + 16, *q_empty = bars + 17;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kMiscOff);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kMiscOff + 4);
+    int *scan = reinterpret_cast<int *>(sm + kMiscOff + 32);
+    int *prefix = reinterpret_cast<int *>(sm + kPrefixOff);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < kKStages; ++i) {
+            mbar_init(&kfull[i], 1);
+            mbar_init(&kempty[i], 1);
+        }
+        for (int i = 0; i < kVStages; ++i) {
+            mbar_init(&vfull[i], 1);
+            mbar_init(&vempty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], 128);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(o_full, 1);
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        tma_prefetch_desc(&qmap);
+        tma_prefetch_desc(&kmap);
+        tma_prefetch_desc(&vmap);
+    }
+    build_item_prefix(a, prefix, scan);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int64_t total_items = prefix[a.batch];
+    uint32_t *fault = &g_prefill_fault;
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        uint32_t jj = 0, qi = 0;
+        bool ok = true;
+        for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
+            const Item I = item_at(u, prefix, a);
+            if (I.bad) {
+                if (lane == 0) record_fault(fault, kFaultRowsMismatch);
+                continue;
+            }
+            if (I.ntiles == 0) continue;
+            if (!mbar_wait(q_empty, (qi & 1) ^ 1, abort_flag, fault)) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(q_full, 2 * kHalf);
+                tma_load_3d(sm + kQOff, &qmap, q_full, 0, I.h, I.q0);
+                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, I.h, I.q0);
+            }
+            __syncwarp();
+            const uint32_t *trow = a.tables + (int64_t)I.b * a.table_stride;
+            for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
+                const int k0 = jt * kPfTile;
+                const int kend = min(I.L, k0 + kPfTile);
+                const int p0 = k0 / a.block_size;
+                const int np = (kend - k0 + a.block_size - 1) / a.block_size;
+                uint32_t pid = 0;
+                bool good = false;
+                if (lane < np) {
+                    const int pi = p0 + lane;
+                    if (pi < a.table_stride) {
+                        pid = __ldg(trow + pi);
+                        good = pid < a.block_count;
+                    }
+                    if (!good) record_fault(fault, kFaultPageOutOfRange);
+                }
+                const unsigned mask = __ballot_sync(0xffffffffu, good);
+                const uint32_t bytes = (uint32_t)__popc(mask) * a.block_size * 256u;
+                const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
+                const int32_t y = (int32_t)pid * a.block_size, x = I.g * 128;
+                const int ks = (int)(jj % kKStages);
+                if (!mbar_wait(&kempty[ks], ((jj / kKStages) & 1) ^ 1, abort_flag, fault)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&kfull[ks], bytes);
+                __syncwarp();
+                if (good) {
+                    unsigned char *kst = sm + kKOff + ks * 32768;
+                    tma_load_2d(kst + ro, &kmap, &kfull[ks], x, y);
+                    tma_load_2d(kst + kHalf + ro, &kmap, &kfull[ks], x + 64, y);
+                }
+                const int vs = (int)(jj % kVStages);
+                if (!mbar_wait(&vempty[vs], ((jj / kVStages) & 1) ^ 1, abort_flag, fault)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&vfull[vs], bytes);
+                __syncwarp();
+                if (good) {
+                    unsigned char *vst = sm + kVOff + vs * 32768;
+                    tma_load_2d(vst + ro, &vmap, &vfull[vs], x, y);
+                    tma_load_2d(vst + kHalf + ro, &vmap, &vfull[vs], x + 64, y);
+                }
+            }
+            ++qi;
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            uint32_t jj = 0, qi = 0;
+            bool ok = true;
+            const uint32_t qaddr = smem_u32(sm + kQOff);
+            // PV of global tile t (jt = its index within its item)
+            auto issue_pv = [&](uint32_t t, int jt, bool precise) -> bool {
+                const int vs = (int)(t % kVStages);
+                if (!mbar_wait(&vfull[vs], (t / kVStages) & 1, abort_flag, fault) ||
+                    !mbar_wait(p_full, t & 1, abort_flag, fault))
+                    return false;
+                tc_fence_after();
+                const uint32_t vaddr = smem_u32(sm + kVOff + vs * 32768);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
+                    mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, bd, kIdescPV,
+                               (jt > 0 || kk > 0) ? 1u : 0u);
+                }
+                if (precise) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
+                        mma_f16_ts(tmem + kColO, tmem + kColPlo + kk * 8, bd, kIdescPV, 1u);
+                    }
+                }
+                mma_commit(o_full);
+                mma_commit(&vempty[vs]);
+                return true;
+            };
+            for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
+                const Item I = item_at(u, prefix, a);
+                if (I.bad || I.ntiles == 0) continue;
+                if (!mbar_wait(q_full, qi & 1, abort_flag, fault)) break;
+                for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
+                    const int ks = (int)(jj % kKStages);
+                    const uint32_t sb = jj & 1;
+                    if (!mbar_wait(&kfull[ks], (jj / kKStages) & 1, abort_flag, fault) ||
+                        !mbar_wait(&s_empty[sb], ((jj >> 1) & 1) ^ 1, abort_flag, fault)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t kaddr = smem_u32(sm + kKOff + ks * 32768);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_desc(qaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                        mma_f16_ss(tmem + kColS + sb * 128, ad, bd, kIdescS, kk > 0);
+                    }
+                    mma_commit(&s_full[sb]);
+                    mma_commit(&kempty[ks]);
+                    if (jt == I.ntiles - 1) mma_commit(q_empty);
+                    if (jt > 0 && !issue_pv(jj - 1, jt - 1, I.precise)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if (ok && !issue_pv(jj - 1, I.ntiles - 1, I.precise)) ok = false;
+                ++qi;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------- softmax -------------------------------
+        // Same loops and the same waits on an abort, minus the TMEM traffic.
+        const int q4 = warp & 3;
+        const int r = q4 * 32 + lane;                 // query row = TMEM lane
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        uint32_t jj = 0;
+        bool aborted = false;
+        for (int64_t u = blockIdx.x; u < total_items; u += gridDim.x) {
+            const Item I = item_at(u, prefix, a);
+            if (I.bad || I.ntiles == 0) continue;
+            const bool row_ok = r < I.nrows;
+            const int pos = I.pos0 + (row_ok ? r : I.nrows - 1);
+            const int limit = a.causal ? min(pos + 1, I.L) : I.L;  // keys < limit attend
+            float m_run = -INFINITY, l = 0.f;
+            for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
+                const uint32_t sb = jj & 1;
+                const int k0 = jt * kPfTile;
+                aborted = aborted || !mbar_wait(&s_full[sb], (jj >> 1) & 1, abort_flag, fault);
+                float s[128];
+                if (!aborted) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(tmem + kColS + sb * 128 + c * 32 + lane_off, v);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]);
+                    }
+                    tmem_wait_ld();
+                    tc_fence_before();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) s[i] = 0.f;
+                }
+                mbar_arrive(&s_empty[sb]);
+                float mx = -INFINITY;
+                const bool masked = k0 + kPfTile > limit;
+#pragma unroll
+                for (int i = 0; i < 128; ++i) {
+                    const float t = s[i] * a.scale_log2;
+                    s[i] = (masked && k0 + i >= limit) ? -INFINITY : t;
+                    mx = fmaxf(mx, s[i]);
+                }
+                float alpha = 1.f;
+                bool rescale = false;
+                if (mx > m_run + kRescaleThreshold) {  // first tile: m_run = -inf
+                    alpha = exp2f(m_run - mx);
+                    m_run = mx;
+                    rescale = jt > 0;
+                    l *= alpha;
+                }
+                // V rows of keys past the sequence may hold anything: zero them
+                // (once their TMA has landed) before the PV MMA reads the tile.
+                if (k0 + kPfTile > I.L) {
+                    const int vs = (int)(jj % kVStages);
+                    aborted = aborted || !mbar_wait(&vfull[vs], (jj / kVStages) & 1, abort_flag, fault);
+                    if (k0 + r >= I.L) {
+                        unsigned char *vrow = sm + kVOff + vs * 32768 + r * 128;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            reinterpret_cast<uint4 *>(vrow)[i] = make_uint4(0, 0, 0, 0);
+                            reinterpret_cast<uint4 *>(vrow + kHalf)[i] = make_uint4(0, 0, 0, 0);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                }
+                // the previous PV must be done before P is overwritten / O rescaled
+                if (jt > 0) aborted = aborted || !mbar_wait(o_full, (jj - 1) & 1, abort_flag, fault);
+                if (!aborted) {
+                    tc_fence_after();
+                    if (rescale) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t v[32];
+                            tmem_ld_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                            tmem_st_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                        }
+                    }
+                }
+                // P = exp2(s - m) in groups of 32 keys: 16 packed columns each
+                float lsum = 0.f;
+#pragma unroll
+                for (int grp = 0; grp < 4; ++grp) {
+                    uint32_t hi[16], lo[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float e0 = exp2f(s[grp * 32 + 2 * i] - m_run);
+                        const float e1 = exp2f(s[grp * 32 + 2 * i + 1] - m_run);
+                        hi[i] = pack2<T>(e0, e1);
+                        const float2 hv = unpack2<T>(hi[i]);
+                        lo[i] = pack2<T>(e0 - hv.x, e1 - hv.y);
+                        lsum += I.precise ? e0 + e1 : hv.x + hv.y;
+                    }
+                    if (!aborted) {
+                        tmem_st_32x32b_x16(tmem + kColP + grp * 16 + lane_off, hi);
+                        if (I.precise) tmem_st_32x32b_x16(tmem + kColPlo + grp * 16 + lane_off, lo);
+                    }
+                }
+                l += lsum;
+                if (!aborted) {
+                    tmem_wait_st();
+                    tc_fence_before();
+                }
+                mbar_arrive(p_full);
+            }
+            // ---- O / l for this item's rows ----
+            aborted = aborted || !mbar_wait(o_full, (jj - 1) & 1, abort_flag, fault);
+            if (!aborted) {
+                tc_fence_after();
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                OT *orow = static_cast<OT *>(a.out) +
+                           ((int64_t)(I.q0 + r) * a.q_heads + I.h) * 128;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                    tmem_wait_ld();
+                    if (row_ok) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            orow[c * 32 + i] = from_f32<OT>(__uint_as_float(v[i]) * inv);
+                    }
+                }
+                tc_fence_before();
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+int g_sms[64];
+int sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (g_sms[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_sms[dev] = n > 0 ? n : 148;
+    }
+    return g_sms[dev];
+}
+
+template <typename T, typename OT>
+int launch(const PfArgs &args, const CUtensorMap &qm, const CUtensorMap &km,
+           const CUtensorMap &vm, cudaStream_t s) {
+    auto kern = paged_prefill_tc_kernel<T, OT>;
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pf_smem_bytes(kPfMaxBatch)) != cudaSuccess)
+            return 0;
+        configured[dev] = 1;
+    }
+    kern<<<sms(), kPfThreads, pf_smem_bytes(args.batch), s>>>(args, qm, km, vm);
+    return cudaGetLastError() == cudaSuccess;
+}
+
 }  // namespace
 }  // namespace pkv
 
@@ -15,11 +542,111 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
                       size_t max_query_len, float scale, int causal, void *output,
                       PkvDType output_dtype, PkvStream stream, char *error,
                       size_t error_capacity) {
-    (void)layer; (void)batch; (void)q_heads; (void)query_offsets; (void)query;
-    (void)total_query_rows; (void)max_query_len; (void)scale; (void)causal; (void)output;
-    (void)output_dtype; (void)stream;
-    pkv_internal_set_error(error, error_capacity, "pkv_paged_prefill: not built yet");
-    return 0;
+    const char *what = "pkv_paged_prefill";
+    if (layer == nullptr || batch == nullptr || query_offsets == nullptr || query == nullptr ||
+        output == nullptr || layer->key_pool == nullptr || layer->value_pool == nullptr ||
+        batch->block_tables == nullptr || batch->seq_lens == nullptr) {
+        pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    if (layer->dtype != PKV_DTYPE_F16 && layer->dtype != PKV_DTYPE_BF16) {
+        pkv_internal_set_error(error, error_capacity, "%s: pool dtype must be F16 or BF16", what);
+        return 0;
+    }
+    if (output_dtype != PKV_DTYPE_F32 && output_dtype != layer->dtype) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: output dtype must be F32 or the pool dtype", what);
+        return 0;
+    }
+    const size_t kvh = layer->kv_heads;
+    const size_t bs = layer->block_size;
+    if (layer->head_dim != 128 || kvh == 0 || q_heads == 0 || q_heads % kvh != 0 ||
+        q_heads > 65535 || (bs != 16 && bs != 32 && bs != 64 && bs != 128)) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: needs head_dim 128, q_heads a multiple of kv_heads and pages "
+                               "of 16, 32, 64 or 128 tokens",
+                               what);
+        return 0;
+    }
+    const uint64_t rows = (uint64_t)layer->block_count * bs;
+    if (batch->batch == 0 || batch->table_stride == 0 || batch->table_stride > INT32_MAX ||
+        rows >= (uint64_t(1) << 31) || total_query_rows >= (size_t(1) << 31) ||
+        !isfinite(scale) || (causal != 0 && causal != 1) || max_query_len > INT32_MAX) {
+        pkv_internal_set_error(error, error_capacity, "%s: invalid batch, table, sizes or scale",
+                               what);
+        return 0;
+    }
+    if (((uintptr_t)layer->key_pool | (uintptr_t)layer->value_pool | (uintptr_t)query) % 16) {
+        pkv_internal_set_error(error, error_capacity, "%s: buffers must be 16-byte aligned", what);
+        return 0;
+    }
+    if (total_query_rows == 0) return 1;
+    auto enc = pkv::encoder();
+    if (enc == nullptr) {
+        pkv_internal_set_error(error, error_capacity, "%s: no tensor-map encoder", what);
+        return 0;
+    }
+    const bool bf16 = layer->dtype == PKV_DTYPE_BF16;
+    const CUtensorMapDataType dt =
+        bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap qm, km, vm;
+    {
+        cuuint64_t dims[3] = {128, q_heads, total_query_rows};
+        cuuint64_t strides[2] = {256, q_heads * 256};
+        cuuint32_t box[3] = {64, 1, 128};
+        cuuint32_t es[3] = {1, 1, 1};
+        if (enc(&qm, dt, 3, const_cast<void *>(query), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            pkv_internal_set_error(error, error_capacity, "%s: query tensor map failed", what);
+            return 0;
+        }
+    }
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[2] = {kvh * 128, rows};
+        cuuint64_t strides[1] = {kvh * 256};
+        cuuint32_t box[2] = {64, (cuuint32_t)bs};
+        cuuint32_t es[2] = {1, 1};
+        if (enc(i == 0 ? &km : &vm, dt, 2, i == 0 ? layer->key_pool : layer->value_pool, dims,
+                strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            pkv_internal_set_error(error, error_capacity, "%s: pool tensor map failed", what);
+            return 0;
+        }
+    }
+    pkv::PfArgs args;
+    args.table_stride = (int32_t)batch->table_stride;
+    args.q_heads = (int32_t)q_heads;
+    args.kv_heads = (int32_t)kvh;
+    args.block_size = (int32_t)bs;
+    args.block_count = (uint32_t)layer->block_count;
+    args.scale_log2 = scale * pkv::kLog2e;
+    args.causal = causal;
+    const cudaStream_t s = (cudaStream_t)stream;
+    int ok = 1;
+    for (size_t b0 = 0; ok && b0 < batch->batch; b0 += pkv::kPfMaxBatch) {
+        const size_t n = batch->batch - b0 < (size_t)pkv::kPfMaxBatch ? batch->batch - b0
+                                                                      : (size_t)pkv::kPfMaxBatch;
+        pkv::PfArgs sl = args;
+        sl.batch = (int32_t)n;
+        sl.tables = batch->block_tables + b0 * batch->table_stride;
+        sl.seq_lens = batch->seq_lens + b0;
+        sl.q_offsets = query_offsets + b0;  // absolute row offsets: query/out stay global
+        sl.out = output;
+        if (!bf16)
+            ok = output_dtype == PKV_DTYPE_F32 ? pkv::launch<__half, float>(sl, qm, km, vm, s)
+                                               : pkv::launch<__half, __half>(sl, qm, km, vm, s);
+        else
+            ok = output_dtype == PKV_DTYPE_F32
+                     ? pkv::launch<__nv_bfloat16, float>(sl, qm, km, vm, s)
+                     : pkv::launch<__nv_bfloat16, __nv_bfloat16>(sl, qm, km, vm, s);
+    }
+    if (!ok) {
+        pkv_internal_set_error(error, error_capacity, "%s: launch failed: %s", what,
+                               cudaGetErrorString(cudaGetLastError()));
+        return 0;
+    }
+    return 1;
 }
 
 int pkv_internal_take_prefill_fault(uint32_t *code) {
