@@ -52,13 +52,16 @@ def parse_args():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[2, 3], default=3)
+    p.add_argument("--config", type=int, choices=[2, 3, 5], default=3)
     p.add_argument("--chunk", type=int, default=0, help="decode split size in tokens (0: auto)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="wall-time budget of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--prefill-batch", type=int, default=0,
+                   help="config 5 only: sequences per step (default: the config's 8; smaller "
+                        "values make small cases for profiling)")
     return p.parse_args()
 
 
@@ -488,9 +491,194 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Config 5: chunked prefill over the paged cache
+# ---------------------------------------------------------------------------
+
+def prefill_flops(past: int, chunk: int, batch: int, q_heads: int, d: int) -> float:
+    """QK^T and PV FLOPs of causal chunked prefill (the chunk sees the past
+    and itself causally)."""
+    return float(batch) * q_heads * 4 * d * (chunk * past + chunk * (chunk + 1) / 2)
+
+
+def measured_peak_tflops() -> tuple[float, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def cfg5_block() -> dict:
+    c = W.CONFIGS[5]
+    return {"workload": c.name, "batch": c.batch, "q_heads": c.q_heads, "kv_heads": c.kv_heads,
+            "head_dim": c.head_dim, "block_size": c.block_size, "storage": "bf16",
+            "accumulate": "f32 (TMEM)", "past": W.CFG5_PAST, "chunk": W.CFG5_CHUNK,
+            "causal": "within the chunk (SDK offset kv_len - q_len)",
+            "parallelism": "one GPU",
+            "l2": "no flush needed: 335 MB of pages + 134 MB of new rows per step (> 126 MB L2)"}
+
+
+def sdk_prefill_rate(budget_s: float, seed: int) -> tuple[float, dict]:
+    """SDK tensor_sdpa_f32 on a slice of config 5: one sequence, one KV head
+    (its 4 query heads), the chunk's last n rows, sized to ~budget_s."""
+    from oracle import oracle as O
+    c = W.CONFIGS[5]
+    threads = cpu_threads()
+    rng = np.random.default_rng(seed + 5)
+    L = W.CFG5_PAST + W.CFG5_CHUNK
+    pages = (L + 15) // 16
+    k = rng.standard_normal((pages * 16, c.kv_width), dtype=np.float32)
+    v = rng.standard_normal((pages * 16, c.kv_width), dtype=np.float32)
+    kb, vb = W.f32_to_bf16_bits(k), W.f32_to_bf16_bits(v)
+    qrows = W.f32_to_bf16_bits(rng.standard_normal((W.CFG5_CHUNK, c.q_heads, c.head_dim),
+                                                   dtype=np.float32))
+    tables = np.arange(pages, dtype=np.uint32)[None, :]
+    group = c.q_heads // c.kv_heads
+
+    def job(rows, kv_n):
+        return O.RefJob("bf16", qrows, np.array([0, W.CFG5_CHUNK], np.int32), kb, vb, c.kv_heads,
+                        c.head_dim, 16, tables, np.array([L]), c.q_heads, c.scale, True,
+                        kv_head0=0, kv_head_n=kv_n, tail_rows=rows)
+
+    probe = job(16, 1)
+    t = probe.run(1)
+    probe.close()
+    rows = int(max(16, min(W.CFG5_CHUNK, 16 * budget_s / max(t, 1e-4))))
+    kv_n = max(1, min(c.kv_heads, threads))
+    j = job(rows, kv_n)
+    sec = j.run(1)  # one tensor_sdpa_f32 call: the SDK CPU path is single-threaded per call
+    j.close()
+    flops = kv_n * group * 4 * c.head_dim * sum(W.CFG5_PAST + W.CFG5_CHUNK - rows + i + 1
+                                               for i in range(rows))
+    info = {"cores": 1, "kind": "reference",
+            "sample": (f"one tensor_sdpa_f32 call (causal) on the last {rows} chunk rows of one "
+                       f"sequence, {kv_n} KV head(s) x {group} query heads; gather+widen untimed")}
+    return flops / sec / 1e12, info
+
+
+def run_prefill(args) -> None:
+    import torch
+
+    import inference_c_b200 as P
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and rank != 0:
+        return  # config 5 is a one-GPU configuration
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    P.load()
+    c = W.CONFIGS[5]
+    B, past, chunk = args.prefill_batch or c.batch, W.CFG5_PAST, W.CFG5_CHUNK
+    L = past + chunk
+    pool_pages = B * ((L + 15) // 16) + 16
+    cache = P.PagedKVCache(16, pool_pages, B)
+    pool = P.PagedPool(cache, local, P.PKV_DTYPE_BF16, 1, c.kv_heads, c.head_dim, B,
+                       (L + 15) // 16 + 1)
+    seqs = [cache.sequence_create() for _ in range(B)]
+    for r in range(1, (past + 15) // 16 + 1):  # interleaved: fragmented tables
+        for s_ in seqs:
+            cache.reserve(s_, min(past, 16 * r))
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    pool.step_begin(seqs, [past] * B)
+    layer = pool.layer(0)
+    kr = torch.randn(B * past, c.kv_width, generator=gen, device=dev).bfloat16()
+    vr = torch.randn(B * past, c.kv_width, generator=gen, device=dev).bfloat16()
+    P.kv_import(layer, pool.step_batch(), kr, vr, pool.step_row_offsets())
+    pool.step_end(True)
+    del kr, vr
+    newk = torch.randn(B * chunk, c.kv_width, generator=gen, device=dev).bfloat16()
+    newv = torch.randn(B * chunk, c.kv_width, generator=gen, device=dev).bfloat16()
+    q = torch.randn(B * chunk, c.q_heads, c.head_dim, generator=gen, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream()
+    steps, warmup = args.steps, args.warmup
+    ea = [torch.cuda.Event(enable_timing=True) for _ in range(4 * steps)]
+
+    def step(i=None):
+        # the SDK transaction for a 2048-token chunk per sequence, rolled back
+        # at the end so every step appends the same chunk at the same positions
+        pool.step_begin(seqs, [chunk] * B)
+        b = pool.step_batch()
+        offs = pool.step_row_offsets()
+        if i is not None:
+            ea[4 * i].record(stream)
+        P.kv_append(layer, b, newk, newv, offs)
+        if i is not None:
+            ea[4 * i + 1].record(stream)
+            ea[4 * i + 2].record(stream)
+        P.paged_prefill(layer, b, q, offs, out, c.scale, chunk, True)
+        if i is not None:
+            ea[4 * i + 3].record(stream)
+        pool.step_end(False)
+
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    with sampler:
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            step(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    fault = P.device_fault(local)
+    if fault:
+        raise SystemExit(f"device fault code {fault} recorded during the bench")
+    ms_step = t0.elapsed_time(t1) / steps
+    app_ms = statistics.mean(ea[4 * i].elapsed_time(ea[4 * i + 1]) for i in range(steps))
+    pf_ms = statistics.mean(ea[4 * i + 2].elapsed_time(ea[4 * i + 3]) for i in range(steps))
+    flops = prefill_flops(past, chunk, B, c.q_heads, c.head_dim)
+    peak, kind = measured_peak_tflops()
+    hbm, hbm_kind = peak_hbm()
+    app_bytes = 2 * 2 * B * chunk * c.kv_width * 2  # K and V rows: read + written
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            rate, info = sdk_prefill_rate(args.cpu_seconds, args.seed)
+            cpu = {"value": rate, "unit": "TFLOP/s", **info}
+        except FileNotFoundError as e:
+            cpu = {"value": None, "unit": "TFLOP/s", "kind": "reference", "cores": 1,
+                   "sample": f"unavailable: {e}"}
+    line = {
+        "metric": "chunked prefill attention TFLOP/s over the paged cache (config 5: append "
+                  "2048-token chunks + causal prefill per step)",
+        "value": flops / (ms_step / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) BF16 Q/K/V on the device",
+        "config": {**cfg5_block(), "batch": B},
+        "tokens_per_s": B * chunk / (ms_step / 1e3),
+        "roofline": {"bound": "tensor", "achieved": flops / (pf_ms / 1e3) / 1e12, "peak": peak,
+                     "unit": "TFLOP/s", "frac": flops / (pf_ms / 1e3) / 1e12 / peak,
+                     "traffic": None, "peak_kind": kind, "kernel": "paged_prefill_tc_kernel",
+                     "algorithmic_flops_per_launch": flops, "mean_launch_ms": pf_ms,
+                     "mma_flops_issued_per_launch": flops * 1.5,
+                     "note": "PV runs twice (16-bit P high and low halves), so the tensor "
+                             "pipe issues 1.5x the algorithmic FLOPs"},
+        "append_roofline": {"bound": "hbm", "achieved": app_bytes / (app_ms / 1e3) / 1e9,
+                            "peak": hbm, "unit": "GB/s",
+                            "frac": app_bytes / (app_ms / 1e3) / 1e9 / hbm,
+                            "kernel": "kv_rows_kernel (append)", "bytes_per_launch": app_bytes,
+                            "mean_launch_ms": app_ms, "peak_kind": hbm_kind},
+        "cpu_baseline": cpu,
+        "e2e": None,
+        "gpu_launches": 3 * steps,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    cache.free()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.config == 5:
+        run_prefill(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -25,7 +25,11 @@
 // max-abs 2e-3 but its tail breaks max-rel 1e-2 on outputs near 1e-2, so the
 // split is kept for every context length (kPreciseKeys above any length).
 // S is double-buffered so the QK^T MMA of tile j+1 overlaps the softmax of
-// tile j.  TMEM columns: S 2 x 128, O 128, P 64, P-low 64 = 512.
+// tile j; P (high half in columns 0-63, low half in 64-127) overwrites the S
+// buffer it was computed from, so P is double-buffered too and the softmax of
+// tile j never waits for the PV MMA of tile j-1 (except to rescale O).  An S
+// buffer is reused for tile j+2 only after the PV of tile j completed.
+// TMEM columns: S/P 2 x 128, O 128 (512 allocated).
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <stdio.h>
@@ -53,7 +57,7 @@ constexpr uint32_t kVOff = kKOff + kKStages * 32768;
 constexpr uint32_t kBarOff = kVOff + kVStages * 32768;
 constexpr uint32_t kMiscOff = kBarOff + 256;
 constexpr uint32_t kPrefixOff = kMiscOff + 256;
-constexpr uint32_t kColS = 0, kColO = 256, kColP = 384, kColPlo = 448, kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 size_t pf_smem_bytes(int batch) { return kPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
@@ -137,6 +141,14 @@ __device__ void build_item_prefix(const PfArgs &a, int *prefix, int *scratch) {
     if (tid == nthr - 1) prefix[a.batch] = before + incl;
 }
 
+// exp2 on the SFU (ex2.approx.ftz): results below 2^-126 flush to zero, far
+// beneath anything a softmax weight can contribute.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <typename T>
 struct Bf16Flag { static constexpr bool value = false; };
 template <>
@@ -178,7 +190,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kBarOff);
     uint64_t *kfull = bars, *kempty = bars + 3, *vfull = bars + 6, *vempty = bars + 8;
-    uint64_t *s_full = bars + 10, *s_empty = bars + 12, *p_full = bars + 14, *o_full = bars + 15;
+    uint64_t *s_full = bars + 10, *pv_done = bars + 12, *p_full = bars + 14;
     uint64_t *q_full = bars + 16, *q_empty = bars + 17;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kMiscOff);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kMiscOff + 4);
@@ -197,10 +209,9 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 128);
+            mbar_init(&pv_done[i], 1);
         }
         mbar_init(p_full, 128);
-        mbar_init(o_full, 1);
         mbar_init(q_full, 1);
         mbar_init(q_empty, 1);
         *abort_flag = 0;
@@ -294,7 +305,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             uint32_t jj = 0, qi = 0;
             bool ok = true;
             const uint32_t qaddr = smem_u32(sm + kQOff);
-            // PV of global tile t (jt = its index within its item)
+            // PV of global tile t (jt = its index within its item); P sits in
+            // the S buffer of t: high half in its columns 0-63, low in 64-127.
             auto issue_pv = [&](uint32_t t, int jt, bool precise) -> bool {
                 const int vs = (int)(t % kVStages);
                 if (!mbar_wait(&vfull[vs], (t / kVStages) & 1, abort_flag, fault) ||
@@ -302,20 +314,21 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     return false;
                 tc_fence_after();
                 const uint32_t vaddr = smem_u32(sm + kVOff + vs * 32768);
+                const uint32_t pcol = tmem + kColS + (t & 1) * 128;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                    mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, bd, kIdescPV,
+                    mma_f16_ts(tmem + kColO, pcol + kk * 8, bd, kIdescPV,
                                (jt > 0 || kk > 0) ? 1u : 0u);
                 }
                 if (precise) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                        mma_f16_ts(tmem + kColO, tmem + kColPlo + kk * 8, bd, kIdescPV, 1u);
+                        mma_f16_ts(tmem + kColO, pcol + 64 + kk * 8, bd, kIdescPV, 1u);
                     }
                 }
-                mma_commit(o_full);
+                mma_commit(&pv_done[t & 1]);
                 mma_commit(&vempty[vs]);
                 return true;
             };
@@ -326,8 +339,9 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
                     const int ks = (int)(jj % kKStages);
                     const uint32_t sb = jj & 1;
+                    // the S buffer is free once the PV of tile jj-2 (its P) is done
                     if (!mbar_wait(&kfull[ks], (jj / kKStages) & 1, abort_flag, fault) ||
-                        !mbar_wait(&s_empty[sb], ((jj >> 1) & 1) ^ 1, abort_flag, fault)) {
+                        !mbar_wait(&pv_done[sb], ((jj >> 1) & 1) ^ 1, abort_flag, fault)) {
                         ok = false;
                         break;
                     }
@@ -382,12 +396,10 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                         for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]);
                     }
                     tmem_wait_ld();
-                    tc_fence_before();
                 } else {
 #pragma unroll
                     for (int i = 0; i < 128; ++i) s[i] = 0.f;
                 }
-                mbar_arrive(&s_empty[sb]);
                 float mx = -INFINITY;
                 const bool masked = k0 + kPfTile > limit;
 #pragma unroll
@@ -399,7 +411,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 float alpha = 1.f;
                 bool rescale = false;
                 if (mx > m_run + kRescaleThreshold) {  // first tile: m_run = -inf
-                    alpha = exp2f(m_run - mx);
+                    alpha = ex2_approx(m_run - mx);
                     m_run = mx;
                     rescale = jt > 0;
                     l *= alpha;
@@ -419,11 +431,12 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     }
                     fence_proxy_async_smem();
                 }
-                // the previous PV must be done before P is overwritten / O rescaled
-                if (jt > 0) aborted = aborted || !mbar_wait(o_full, (jj - 1) & 1, abort_flag, fault);
-                if (!aborted) {
-                    tc_fence_after();
-                    if (rescale) {
+                // rescaling O needs the previous tile's PV to be done
+                if (rescale) {
+                    aborted = aborted ||
+                              !mbar_wait(&pv_done[(jj - 1) & 1], ((jj - 1) >> 1) & 1, abort_flag, fault);
+                    if (!aborted) {
+                        tc_fence_after();
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             uint32_t v[32];
@@ -436,23 +449,24 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                         }
                     }
                 }
-                // P = exp2(s - m) in groups of 32 keys: 16 packed columns each
+                // P = exp2(s - m) over S's own columns: high half 0-63, low 64-127
                 float lsum = 0.f;
+                const uint32_t pcol = tmem + kColS + sb * 128 + lane_off;
 #pragma unroll
                 for (int grp = 0; grp < 4; ++grp) {
                     uint32_t hi[16], lo[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float e0 = exp2f(s[grp * 32 + 2 * i] - m_run);
-                        const float e1 = exp2f(s[grp * 32 + 2 * i + 1] - m_run);
+                        const float e0 = ex2_approx(s[grp * 32 + 2 * i] - m_run);
+                        const float e1 = ex2_approx(s[grp * 32 + 2 * i + 1] - m_run);
                         hi[i] = pack2<T>(e0, e1);
                         const float2 hv = unpack2<T>(hi[i]);
                         lo[i] = pack2<T>(e0 - hv.x, e1 - hv.y);
                         lsum += I.precise ? e0 + e1 : hv.x + hv.y;
                     }
                     if (!aborted) {
-                        tmem_st_32x32b_x16(tmem + kColP + grp * 16 + lane_off, hi);
-                        if (I.precise) tmem_st_32x32b_x16(tmem + kColPlo + grp * 16 + lane_off, lo);
+                        tmem_st_32x32b_x16(pcol + grp * 16, hi);
+                        if (I.precise) tmem_st_32x32b_x16(pcol + 64 + grp * 16, lo);
                     }
                 }
                 l += lsum;
@@ -463,7 +477,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 mbar_arrive(p_full);
             }
             // ---- O / l for this item's rows ----
-            aborted = aborted || !mbar_wait(o_full, (jj - 1) & 1, abort_flag, fault);
+            aborted = aborted ||
+                      !mbar_wait(&pv_done[(jj - 1) & 1], ((jj - 1) >> 1) & 1, abort_flag, fault);
             if (!aborted) {
                 tc_fence_after();
                 const float inv = l > 0.f ? 1.f / l : 0.f;
