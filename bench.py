@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[2, 3, 5], default=3)
+    p.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3)
     p.add_argument("--chunk", type=int, default=0, help="decode split size in tokens (0: auto)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -674,8 +674,189 @@ def run_prefill(args) -> None:
     cache.free()
 
 
+# ---------------------------------------------------------------------------
+# Config 4: one 131072-token sequence, KV heads split across the GPUs
+# ---------------------------------------------------------------------------
+
+def run_cfg4(args) -> None:
+    import torch
+
+    import inference_c_b200 as P
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    c = W.CONFIGS[4]
+    if c.kv_heads % world:
+        raise SystemExit(f"config 4 splits {c.kv_heads} KV heads; --gpus must divide it")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    P.load()
+    kvl = c.kv_heads // world                 # KV heads owned by this rank
+    qhl = kvl * (c.q_heads // c.kv_heads)     # their query heads
+    steps, warmup = args.steps, args.warmup
+    grow = 2 * warmup + 2 * steps + 2
+    L0 = W.CFG4_TOKENS
+    need = (L0 + grow + 15) // 16
+    rng = np.random.default_rng(args.seed + 4)
+    gaps = rng.integers(0, 4, need)           # filler pages before each real page
+    pool_pages = need + int(gaps.sum()) + 16
+    cache = P.PagedKVCache(16, pool_pages, 2)
+    pool = P.PagedPool(cache, local, P.PKV_DTYPE_F16, 1, kvl, c.head_dim, 1, need + 1)
+    seq, filler = cache.sequence_create(), cache.sequence_create()
+    have_f = 0
+    for i in range(need):  # same seeded interleaving on every rank: identical tables
+        have_f += int(gaps[i])
+        if gaps[i]:
+            assert cache.reserve(filler, 16 * have_f)
+        assert cache.reserve(seq, 16 * (i + 1))
+    assert cache.release(filler)
+    cache.set_length(seq, 0)
+    cache.reserve(seq, L0)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
+    pool.step_begin([seq], [L0])
+    layer = pool.layer(0)
+    kv = kvl * c.head_dim
+    for start in range(0, L0, 32768):  # this rank's heads only
+        n = min(32768, L0 - start)
+        kr = torch.randn(n, kv, generator=gen, device=dev).half()
+        vr = torch.randn(n, kv, generator=gen, device=dev).half()
+        offs = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        b = pool.step_batch()
+        lens = torch.tensor([start + n], dtype=torch.int32, device=dev)
+        P.kv_append(layer, P.PkvBatch(b.block_tables, b.table_stride, lens.data_ptr(), 1), kr,
+                    vr, offs)
+        torch.cuda.synchronize()
+    pool.step_end(True)
+    q = torch.randn(1, qhl, c.head_dim, generator=gen, device=dev).half()
+    newk = torch.randn(1, kv, generator=gen, device=dev).half()
+    newv = torch.randn(1, kv, generator=gen, device=dev).half()
+    out = torch.empty(1, qhl, c.head_dim, dtype=torch.float16, device=dev)
+    full = torch.empty(world, qhl, c.head_dim, dtype=torch.float16, device=dev)
+    max_len = L0 + grow
+    ws = P.decode_workspace(1, qhl, c.head_dim, max_len, device=dev)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4 * steps)]
+    cur = [L0]
+
+    def step(i=None, q_in=None):
+        pool.step_begin([seq], [1])
+        b = pool.step_batch()
+        P.kv_append(layer, b, newk, newv)
+        if i is not None:
+            ev[4 * i].record(stream)
+        P.paged_decode(layer, b, q if q_in is None else q_in, out, c.scale, max_len, ws)
+        if i is not None:
+            ev[4 * i + 1].record(stream)
+        pool.step_end(True)
+        cur[0] += 1
+        if dist is not None:
+            if i is not None:
+                ev[4 * i + 2].record(stream)
+            dist.all_gather_into_tensor(full, out)  # per-head outputs over NVLink
+            if i is not None:
+                ev[4 * i + 3].record(stream)
+        else:
+            full.copy_(out)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    with sampler:
+        for _ in range(warmup):
+            step()
+        barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            step(i)
+        t1.record(stream)
+        barrier()
+        ms = max_over_ranks(t0.elapsed_time(t1) / steps)
+        dec = statistics.mean(ev[4 * i].elapsed_time(ev[4 * i + 1]) for i in range(steps))
+        ag = (statistics.mean(ev[4 * i + 2].elapsed_time(ev[4 * i + 3]) for i in range(steps))
+              if dist is not None else 0.0)
+        h_q = torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
+        h_k = torch.empty(newk.shape, dtype=newk.dtype, pin_memory=True).copy_(newk.cpu())
+        h_v = torch.empty(newv.shape, dtype=newv.dtype, pin_memory=True).copy_(newv.cpu())
+        h_o = torch.empty(full.shape, dtype=full.dtype, pin_memory=True)
+        dq = torch.empty_like(q)
+
+        def e2e_step():
+            dq.copy_(h_q, non_blocking=True)
+            newk.copy_(h_k, non_blocking=True)
+            newv.copy_(h_v, non_blocking=True)
+            step(None, dq)
+            h_o.copy_(full, non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(warmup):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    fault = P.device_fault(local)
+    if fault:
+        raise SystemExit(f"device fault code {fault} recorded during the bench")
+    peak, peak_kind = peak_hbm()
+    alg = (L0 + warmup + steps) * kv * 2 * 2 + 2 * q.numel() * 2
+    gbs = alg / (dec / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "paged decode attention tokens/s (config 4: one 131072-token sequence, "
+                      "KV heads split across GPUs, NCCL all-gather of per-head outputs)",
+            "value": 1.0 / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic: seeded N(0,1) FP16 on the device; seeded fragmented block table",
+            "config": {"workload": c.name, "tokens": L0, "q_heads": c.q_heads,
+                       "kv_heads": c.kv_heads, "head_dim": c.head_dim, "block_size": 16,
+                       "kv_heads_per_gpu": kvl,
+                       "parallelism": f"KV-head split over {world} GPU(s) + NCCL all-gather",
+                       "l2": "no flush needed: 512 MiB of pages per step at one GPU"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "paged_decode_tc_kernel (+ merge kernel when split wide)",
+                         "algorithmic_bytes_per_launch": alg, "mean_launch_ms": dec},
+            "allgather_ms": ag,
+            "cpu_baseline": None,
+            "e2e": {"value": 1.0 / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": (h_q.numel() + h_k.numel() + h_v.numel()) * 2 * world,
+                    "d2h_bytes_per_step": h_o.numel() * 2},
+            "gpu_launches": steps * (3 + (1 if dist is not None else 0)),
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    cache.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
+    if args.config == 4:
+        run_cfg4(args)
+        return
     if args.config == 5:
         run_prefill(args)
     elif args.impl == "reference":

@@ -1,7 +1,7 @@
 // pkv_sm100.cuh -- thin inline-PTX wrappers for the sm_100a building blocks
 // used by the paged attention kernels: mbarriers (with bounded waits), TMA
 // tile loads, tcgen05 MMA / TMEM management and the shared-memory matrix
-// descriptors.  No loads here ever use cluster multicast.
+// descriptors.  Every TMA load here targets this CTA's own shared memory.
 #pragma once
 
 #include <cuda.h>
