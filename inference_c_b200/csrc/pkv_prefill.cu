@@ -5,31 +5,30 @@
 // 0 .. L_b - n_b + j, the SDK's causal offset kv_len - q_len
 // (attention.c:251, :352-353), otherwise to all L_b keys.
 //
-// Work item = (sequence, query head, tile of 128 query rows).  One persistent
-// 192-thread CTA per SM, warp-specialised:
-//   warp 0     producer: TMA-loads the item's 128 query rows (a 3-D box over
-//              [rows][heads][128]) and, per 128-key tile, every page of K and
-//              V for the item's KV head straight from the pool (2-D boxes of
-//              one page x 64 columns); K ring of 3 and V ring of 2 stages;
-//   warp 1     one thread issues tcgen05.mma:
-//                S[128 q][128 k]  = Q[128][128] . K^T            (smem x smem)
-//                O[128 q][128 d] += P[128 q][128 k] . V[128 k][128] (P from TMEM)
-//   warps 2-5  softmax: thread r owns query row r (TMEM lane r), so the row
-//              max and sum need no cross-thread reduction.  P goes back to
-//              TMEM as packed 16-bit pairs and feeds the PV MMA directly.
-// O accumulates in TMEM (FP32).  The running max is only raised when a tile's
-// max exceeds it by more than 2^8 (lazy rescale: O is rescaled in TMEM only
-// on those tiles).  P is written as a 16-bit high half and a low half
-// (p - round(p)), and a second PV MMA adds the low half: with P rounded to
-// bf16 alone the output error (~1e-4 absolute at 2k-10k keys) stays inside
-// max-abs 2e-3 but its tail breaks max-rel 1e-2 on outputs near 1e-2, so the
-// split is kept for every context length (kPreciseKeys above any length).
-// S is double-buffered so the QK^T MMA of tile j+1 overlaps the softmax of
-// tile j; P (high half in columns 0-63, low half in 64-127) overwrites the S
-// buffer it was computed from, so P is double-buffered too and the softmax of
-// tile j never waits for the PV MMA of tile j-1 (except to rescale O).  An S
-// buffer is reused for tile j+2 only after the PV of tile j completed.
-// TMEM columns: S/P 2 x 128, O 128 (512 allocated).
+// Work item = 128 query rows of two query heads of the same KV head (one head
+// when the GQA group is odd).  One persistent 384-thread CTA per SM:
+//   warp 0       producer: TMA-loads the item's query rows of both heads
+//                (3-D boxes over [rows][heads][128]) and, per 128-key tile,
+//                every page of K and V of the KV head straight from the pool
+//                (2-D boxes of one page x 64 columns); K and V rings of 2;
+//   warp 1       one thread issues tcgen05.mma, interleaving the two heads
+//                so each softmax group works while the tensor cores serve
+//                the other:  S_A(j), PV_B(j-1), S_B(j), PV_A(j), ...
+//                  S[128 q][128 k]  = Q[128][128] . K^T          (smem x smem)
+//                  O[128 q][128 d] += P[128 q][128 k] . V[128][128] (P in TMEM)
+//   warps 4-7    softmax of head A, warps 8-11 softmax of head B: thread r
+//                owns query row r (TMEM lane r), so row max and sum need no
+//                cross-thread traffic.  Two passes over S in TMEM (max, then
+//                exp) keep 32 scores in registers at a time.
+// Each head's P replaces its S in TMEM as 16-bit pairs, a high half and a
+// low half (p - round(p)) per 32-key chunk, and feeds the PV MMA as the
+// A operand (two MMAs: high then low); with P rounded to bf16 alone the
+// output error (~1e-4 at 2k-10k keys) passes max-abs 2e-3 but its tail
+// breaks max-rel 1e-2 on outputs near 1e-2, so the split is always on.
+// O accumulates in TMEM (FP32); the running max is raised only when a tile's
+// max exceeds it by more than 2^8 (lazy rescale of O in TMEM).  A head's S/P
+// buffer is reused for its next tile only after its PV completed.  TMEM:
+// head A S/P 0-127, O 128-255; head B S/P 256-383, O 384-511.
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <stdio.h>
@@ -43,21 +42,19 @@ namespace {
 
 __device__ uint32_t g_prefill_fault;
 
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 384;
 constexpr int kPfTile = 128;
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr int kStages = 2;                // K ring and V ring depth
 constexpr int kPfMaxBatch = 512;
-constexpr int kPreciseKeys = 1 << 30;  // hi/lo P for every length (see above)
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 constexpr uint32_t kHalf = 16384;         // 128 rows x 128 bytes
-constexpr uint32_t kQOff = 0;             // Q [2 halves][128][64]
-constexpr uint32_t kKOff = 32768;         // K stages of 32 KiB
-constexpr uint32_t kVOff = kKOff + kKStages * 32768;
-constexpr uint32_t kBarOff = kVOff + kVStages * 32768;
+constexpr uint32_t kQOff = 0;             // Q of head A then head B, [2 halves][128][64] each
+constexpr uint32_t kKOff = 65536;         // K stages of 32 KiB
+constexpr uint32_t kVOff = kKOff + kStages * 32768;
+constexpr uint32_t kBarOff = kVOff + kStages * 32768;
 constexpr uint32_t kMiscOff = kBarOff + 256;
 constexpr uint32_t kPrefixOff = kMiscOff + 256;
-constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
+constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
 size_t pf_smem_bytes(int batch) { return kPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
@@ -75,12 +72,18 @@ struct PfArgs {
     uint32_t block_count;
     float scale_log2;
     int32_t causal;
+    int32_t paired;  // GQA group even: items carry two heads
 };
 
 struct Item {
-    int b, h, g, q0, nrows, L, pos0, ntiles;
-    bool precise, bad;
+    int b, h0, g, q0, nrows, L, pos0, ntiles;
+    bool bad;
 };
+
+__device__ __forceinline__ int items_per_qtile(const PfArgs &a) {
+    const int group = a.q_heads / a.kv_heads;
+    return a.kv_heads * (a.paired ? group / 2 : group);
+}
 
 __device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfArgs &a) {
     Item I;
@@ -93,10 +96,14 @@ __device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfAr
     const int qstart = __ldg(a.q_offsets + lo);
     const int nq = __ldg(a.q_offsets + lo + 1) - qstart;
     const int nqt = (nq + kPfTile - 1) / kPfTile;
+    const int per = items_per_qtile(a);
     const int w = (int)(u - prefix[lo]);
-    const int qt = nqt - 1 - w / a.q_heads;  // longest tiles of a sequence first
-    I.h = w - (w / a.q_heads) * a.q_heads;
-    I.g = I.h / (a.q_heads / a.kv_heads);
+    const int qt = nqt - 1 - w / per;  // longest tiles of a sequence first
+    const int rest = w - (w / per) * per;
+    const int group = a.q_heads / a.kv_heads;
+    const int np = a.paired ? group / 2 : group;
+    I.g = rest / np;
+    I.h0 = I.g * group + (rest - I.g * np) * (a.paired ? 2 : 1);
     I.q0 = qstart + qt * kPfTile;
     I.nrows = min(kPfTile, nq - qt * kPfTile);
     I.L = __ldg(a.seq_lens + lo);
@@ -104,19 +111,19 @@ __device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfAr
     I.pos0 = I.L - nq + qt * kPfTile;
     const int kmax = a.causal ? min(I.L, I.pos0 + I.nrows) : I.L;
     I.ntiles = I.bad ? 0 : (kmax + kPfTile - 1) / kPfTile;
-    I.precise = kmax < kPreciseKeys;
     return I;
 }
 
 __device__ void build_item_prefix(const PfArgs &a, int *prefix, int *scratch) {
     const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (a.batch + nthr - 1) / nthr;
+    const int items = items_per_qtile(a);
     int local = 0;
     for (int k = 0; k < per; ++k) {
         const int b = tid * per + k;
         if (b < a.batch) {
             const int nq = __ldg(a.q_offsets + b + 1) - __ldg(a.q_offsets + b);
-            local += (max(nq, 0) + kPfTile - 1) / kPfTile * a.q_heads;
+            local += (max(nq, 0) + kPfTile - 1) / kPfTile * items;
         }
     }
     int incl = local;
@@ -135,7 +142,7 @@ __device__ void build_item_prefix(const PfArgs &a, int *prefix, int *scratch) {
         if (b < a.batch) {
             prefix[b] = run;
             const int nq = __ldg(a.q_offsets + b + 1) - __ldg(a.q_offsets + b);
-            run += (max(nq, 0) + kPfTile - 1) / kPfTile * a.q_heads;
+            run += (max(nq, 0) + kPfTile - 1) / kPfTile * items;
         }
     }
     if (tid == nthr - 1) prefix[a.batch] = before + incl;
@@ -177,6 +184,30 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
     return __half22float2(*reinterpret_cast<__half2 *>(&v));
 }
 
+// 32 FP32 accumulator words of one output row, times `inv`, as 16-byte stores.
+template <typename OT>
+__device__ __forceinline__ void store_row32(OT *dst, const uint32_t (&v)[32], float inv);
+template <>
+__device__ __forceinline__ void store_row32<float>(float *dst, const uint32_t (&v)[32], float inv) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        reinterpret_cast<float4 *>(dst)[i] =
+            make_float4(__uint_as_float(v[4 * i]) * inv, __uint_as_float(v[4 * i + 1]) * inv,
+                        __uint_as_float(v[4 * i + 2]) * inv, __uint_as_float(v[4 * i + 3]) * inv);
+}
+template <typename OT>
+__device__ __forceinline__ void store_row32(OT *dst, const uint32_t (&v)[32], float inv) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint4 w;
+        w.x = pack2<OT>(__uint_as_float(v[8 * i]) * inv, __uint_as_float(v[8 * i + 1]) * inv);
+        w.y = pack2<OT>(__uint_as_float(v[8 * i + 2]) * inv, __uint_as_float(v[8 * i + 3]) * inv);
+        w.z = pack2<OT>(__uint_as_float(v[8 * i + 4]) * inv, __uint_as_float(v[8 * i + 5]) * inv);
+        w.w = pack2<OT>(__uint_as_float(v[8 * i + 6]) * inv, __uint_as_float(v[8 * i + 7]) * inv);
+        reinterpret_cast<uint4 *>(dst)[i] = w;
+    }
+}
+
 template <typename T, typename OT>
 __global__ void __launch_bounds__(kPfThreads, 1)
 paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap,
@@ -189,29 +220,28 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
     unsigned char *sm = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kBarOff);
-    uint64_t *kfull = bars, *kempty = bars + 3, *vfull = bars + 6, *vempty = bars + 8;
-    uint64_t *s_full = bars + 10, *pv_done = bars + 12, *p_full = bars + 14;
-    uint64_t *q_full = bars + 16, *q_empty = bars + 17;
+    uint64_t *kfull = bars, *kempty = bars + 2, *vfull = bars + 4, *vempty = bars + 6;
+    uint64_t *s_full = bars + 8, *p_full = bars + 10, *pv_done = bars + 12;  // [head A, head B]
+    uint64_t *q_full = bars + 14, *q_empty = bars + 15;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kMiscOff);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kMiscOff + 4);
-    int *scan = reinterpret_cast<int *>(sm + kMiscOff + 32);
+    int *scan = reinterpret_cast<int *>(sm + kMiscOff + 32);  // 12 ints
     int *prefix = reinterpret_cast<int *>(sm + kPrefixOff);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool paired = a.paired != 0;
     if (tid == 0) {
-        for (int i = 0; i < kKStages; ++i) {
+        for (int i = 0; i < kStages; ++i) {
             mbar_init(&kfull[i], 1);
             mbar_init(&kempty[i], 1);
-        }
-        for (int i = 0; i < kVStages; ++i) {
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&pv_done[i], 1);
+        for (int w = 0; w < 2; ++w) {
+            mbar_init(&s_full[w], 1);
+            mbar_init(&p_full[w], 128);
+            mbar_init(&pv_done[w], 1);
         }
-        mbar_init(p_full, 128);
         mbar_init(q_full, 1);
         mbar_init(q_empty, 1);
         *abort_flag = 0;
@@ -247,9 +277,13 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             if (I.ntiles == 0) continue;
             if (!mbar_wait(q_empty, (qi & 1) ^ 1, abort_flag, fault)) break;
             if (lane == 0) {
-                mbar_arrive_expect_tx(q_full, 2 * kHalf);
-                tma_load_3d(sm + kQOff, &qmap, q_full, 0, I.h, I.q0);
-                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, I.h, I.q0);
+                mbar_arrive_expect_tx(q_full, (paired ? 4u : 2u) * kHalf);
+                tma_load_3d(sm + kQOff, &qmap, q_full, 0, I.h0, I.q0);
+                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, I.h0, I.q0);
+                if (paired) {
+                    tma_load_3d(sm + kQOff + 2 * kHalf, &qmap, q_full, 0, I.h0 + 1, I.q0);
+                    tma_load_3d(sm + kQOff + 3 * kHalf, &qmap, q_full, 64, I.h0 + 1, I.q0);
+                }
             }
             __syncwarp();
             const uint32_t *trow = a.tables + (int64_t)I.b * a.table_stride;
@@ -272,29 +306,29 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 const uint32_t bytes = (uint32_t)__popc(mask) * a.block_size * 256u;
                 const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
                 const int32_t y = (int32_t)pid * a.block_size, x = I.g * 128;
-                const int ks = (int)(jj % kKStages);
-                if (!mbar_wait(&kempty[ks], ((jj / kKStages) & 1) ^ 1, abort_flag, fault)) {
+                const int st = (int)(jj % kStages);
+                const uint32_t par = ((jj / kStages) & 1) ^ 1;
+                if (!mbar_wait(&kempty[st], par, abort_flag, fault)) {
                     ok = false;
                     break;
                 }
-                if (lane == 0) mbar_arrive_expect_tx(&kfull[ks], bytes);
+                if (lane == 0) mbar_arrive_expect_tx(&kfull[st], bytes);
                 __syncwarp();
                 if (good) {
-                    unsigned char *kst = sm + kKOff + ks * 32768;
-                    tma_load_2d(kst + ro, &kmap, &kfull[ks], x, y);
-                    tma_load_2d(kst + kHalf + ro, &kmap, &kfull[ks], x + 64, y);
+                    unsigned char *kst = sm + kKOff + st * 32768;
+                    tma_load_2d(kst + ro, &kmap, &kfull[st], x, y);
+                    tma_load_2d(kst + kHalf + ro, &kmap, &kfull[st], x + 64, y);
                 }
-                const int vs = (int)(jj % kVStages);
-                if (!mbar_wait(&vempty[vs], ((jj / kVStages) & 1) ^ 1, abort_flag, fault)) {
+                if (!mbar_wait(&vempty[st], par, abort_flag, fault)) {
                     ok = false;
                     break;
                 }
-                if (lane == 0) mbar_arrive_expect_tx(&vfull[vs], bytes);
+                if (lane == 0) mbar_arrive_expect_tx(&vfull[st], bytes);
                 __syncwarp();
                 if (good) {
-                    unsigned char *vst = sm + kVOff + vs * 32768;
-                    tma_load_2d(vst + ro, &vmap, &vfull[vs], x, y);
-                    tma_load_2d(vst + kHalf + ro, &vmap, &vfull[vs], x + 64, y);
+                    unsigned char *vst = sm + kVOff + st * 32768;
+                    tma_load_2d(vst + ro, &vmap, &vfull[st], x, y);
+                    tma_load_2d(vst + kHalf + ro, &vmap, &vfull[st], x + 64, y);
                 }
             }
             ++qi;
@@ -304,74 +338,90 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
         if (lane == 0) {
             uint32_t jj = 0, qi = 0;
             bool ok = true;
-            const uint32_t qaddr = smem_u32(sm + kQOff);
-            // PV of global tile t (jt = its index within its item); P sits in
-            // the S buffer of t: high half in its columns 0-63, low in 64-127.
-            auto issue_pv = [&](uint32_t t, int jt, bool precise) -> bool {
-                const int vs = (int)(t % kVStages);
-                if (!mbar_wait(&vfull[vs], (t / kVStages) & 1, abort_flag, fault) ||
-                    !mbar_wait(p_full, t & 1, abort_flag, fault))
+            // Paired: head w owns S/P buffer w and O buffer w.  Unpaired: the
+            // one head alternates S/P buffers by tile and accumulates in O 0.
+            auto sbuf = [&](int w, uint32_t t) -> uint32_t {
+                return tmem + (paired ? (uint32_t)w : (t & 1u)) * 256u;
+            };
+            // S of head w for global tile t.  Its S/P buffer is free once the
+            // PV that last read it completed: tile t-1 of the head (paired),
+            // tile t-2 (unpaired).
+            auto issue_s = [&](int w, uint32_t t) -> bool {
+                if (paired || t >= 2) {
+                    const uint32_t par = paired ? (t & 1) ^ 1 : (t & 1);
+                    if (!mbar_wait(&pv_done[w], par, abort_flag, fault)) return false;
+                }
+                tc_fence_after();
+                const uint32_t qaddr = smem_u32(sm + kQOff + w * 2 * kHalf);
+                const uint32_t kaddr = smem_u32(sm + kKOff + (t % kStages) * 32768);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t ad = sw128_desc(qaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                    mma_f16_ss(sbuf(w, t), ad, bd, kIdescS, kk > 0);
+                }
+                mma_commit(&s_full[w]);
+                return true;
+            };
+            // PV of head w for global tile t (jt: its index within the item),
+            // then release the tile's V stage when no other head still reads it.
+            // P of 32-key chunk c: high half in columns 32c..32c+15, low half
+            // in 32c+16..32c+31 of the S/P buffer.
+            auto issue_pv = [&](int w, uint32_t t, int jt, bool last_reader) -> bool {
+                const int st = (int)(t % kStages);
+                if (!mbar_wait(&vfull[st], (t / kStages) & 1, abort_flag, fault) ||
+                    !mbar_wait(&p_full[w], t & 1, abort_flag, fault))
                     return false;
                 tc_fence_after();
-                const uint32_t vaddr = smem_u32(sm + kVOff + vs * 32768);
-                const uint32_t pcol = tmem + kColS + (t & 1) * 128;
+                const uint32_t vaddr = smem_u32(sm + kVOff + st * 32768);
+                const uint32_t pcol = sbuf(w, t);
+                const uint32_t ocol = tmem + (paired ? (uint32_t)w * 256u : 0u) + 128u;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                    mma_f16_ts(tmem + kColO, pcol + kk * 8, bd, kIdescPV,
+                    mma_f16_ts(ocol, pcol + (kk >> 1) * 32 + (kk & 1) * 8, bd, kIdescPV,
                                (jt > 0 || kk > 0) ? 1u : 0u);
                 }
-                if (precise) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                        mma_f16_ts(tmem + kColO, pcol + 64 + kk * 8, bd, kIdescPV, 1u);
-                    }
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
+                    mma_f16_ts(ocol, pcol + (kk >> 1) * 32 + 16 + (kk & 1) * 8, bd, kIdescPV, 1u);
                 }
-                mma_commit(&pv_done[t & 1]);
-                mma_commit(&vempty[vs]);
+                mma_commit(&pv_done[w]);
+                if (last_reader) mma_commit(&vempty[st]);
                 return true;
             };
+            // Issue order per tile j: paired  S_A(j) PV_B(j-1) S_B(j) PV_A(j);
+            //                         unpaired S(j) PV(j-1).
+            // Each softmax group works while the tensor pipe serves the other.
             for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
                 const Item I = item_at(u, prefix, a);
                 if (I.bad || I.ntiles == 0) continue;
                 if (!mbar_wait(q_full, qi & 1, abort_flag, fault)) break;
-                for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
-                    const int ks = (int)(jj % kKStages);
-                    const uint32_t sb = jj & 1;
-                    // the S buffer is free once the PV of tile jj-2 (its P) is done
-                    if (!mbar_wait(&kfull[ks], (jj / kKStages) & 1, abort_flag, fault) ||
-                        !mbar_wait(&pv_done[sb], ((jj >> 1) & 1) ^ 1, abort_flag, fault)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t kaddr = smem_u32(sm + kKOff + ks * 32768);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t ad = sw128_desc(qaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-                        mma_f16_ss(tmem + kColS + sb * 128, ad, bd, kIdescS, kk > 0);
-                    }
-                    mma_commit(&s_full[sb]);
-                    mma_commit(&kempty[ks]);
+                for (int jt = 0; jt < I.ntiles && ok; ++jt, ++jj) {
+                    const int st = (int)(jj % kStages);
+                    ok = mbar_wait(&kfull[st], (jj / kStages) & 1, abort_flag, fault) &&
+                         issue_s(0, jj);
+                    if (ok && jt > 0) ok = issue_pv(paired ? 1 : 0, jj - 1, jt - 1, true);
+                    if (ok && paired) ok = issue_s(1, jj);
+                    if (!ok) break;
+                    mma_commit(&kempty[st]);
                     if (jt == I.ntiles - 1) mma_commit(q_empty);
-                    if (jt > 0 && !issue_pv(jj - 1, jt - 1, I.precise)) {
-                        ok = false;
-                        break;
-                    }
+                    if (paired) ok = issue_pv(0, jj, jt, false);
                 }
-                if (ok && !issue_pv(jj - 1, I.ntiles - 1, I.precise)) ok = false;
+                if (ok) ok = issue_pv(paired ? 1 : 0, jj - 1, I.ntiles - 1, true);
                 ++qi;
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp >= 4 && (warp < 8 || paired)) {
         // ------------------------------- softmax -------------------------------
         // Same loops and the same waits on an abort, minus the TMEM traffic.
+        const int w = warp < 8 ? 0 : 1;         // head A or head B
         const int q4 = warp & 3;
-        const int r = q4 * 32 + lane;                 // query row = TMEM lane
+        const int r = q4 * 32 + lane;            // query row = TMEM lane
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        const uint32_t ocol = tmem + w * 256 + 128 + lane_off;
         uint32_t jj = 0;
         bool aborted = false;
         for (int64_t u = blockIdx.x; u < total_items; u += gridDim.x) {
@@ -382,32 +432,30 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             const int limit = a.causal ? min(pos + 1, I.L) : I.L;  // keys < limit attend
             float m_run = -INFINITY, l = 0.f;
             for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
-                const uint32_t sb = jj & 1;
                 const int k0 = jt * kPfTile;
-                aborted = aborted || !mbar_wait(&s_full[sb], (jj >> 1) & 1, abort_flag, fault);
-                float s[128];
-                if (!aborted) {
-                    tc_fence_after();
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t v[32];
-                        tmem_ld_32x32b_x32(tmem + kColS + sb * 128 + c * 32 + lane_off, v);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]);
-                    }
-                    tmem_wait_ld();
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 128; ++i) s[i] = 0.f;
-                }
-                float mx = -INFINITY;
                 const bool masked = k0 + kPfTile > limit;
+                const uint32_t scol = tmem + (paired ? (uint32_t)w : (jj & 1u)) * 256u + lane_off;
+                aborted = aborted || !mbar_wait(&s_full[w], jj & 1, abort_flag, fault);
+                if (!aborted) tc_fence_after();
+                // pass 1: row max
+                float mx = -INFINITY;
 #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    const float t = s[i] * a.scale_log2;
-                    s[i] = (masked && k0 + i >= limit) ? -INFINITY : t;
-                    mx = fmaxf(mx, s[i]);
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t v[32];
+                    if (!aborted) {
+                        tmem_ld_32x32b_x32(scol + c * 32, v);
+                        tmem_wait_ld();
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = 0u;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const bool dead = masked && k0 + c * 32 + i >= limit;
+                        mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(v[i]));
+                    }
                 }
+                mx *= a.scale_log2;  // scale > 0 commutes with max
                 float alpha = 1.f;
                 bool rescale = false;
                 if (mx > m_run + kRescaleThreshold) {  // first tile: m_run = -inf
@@ -416,13 +464,13 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     rescale = jt > 0;
                     l *= alpha;
                 }
-                // V rows of keys past the sequence may hold anything: zero them
-                // (once their TMA has landed) before the PV MMA reads the tile.
-                if (k0 + kPfTile > I.L) {
-                    const int vs = (int)(jj % kVStages);
-                    aborted = aborted || !mbar_wait(&vfull[vs], (jj / kVStages) & 1, abort_flag, fault);
+                // V rows of keys past the sequence may hold anything: head A
+                // zeroes them (once their TMA landed) before either PV reads.
+                if (w == 0 && k0 + kPfTile > I.L) {
+                    const int st = (int)(jj % kStages);
+                    aborted = aborted || !mbar_wait(&vfull[st], (jj / kStages) & 1, abort_flag, fault);
                     if (k0 + r >= I.L) {
-                        unsigned char *vrow = sm + kVOff + vs * 32768 + r * 128;
+                        unsigned char *vrow = sm + kVOff + st * 32768 + r * 128;
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             reinterpret_cast<uint4 *>(vrow)[i] = make_uint4(0, 0, 0, 0);
@@ -431,42 +479,51 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     }
                     fence_proxy_async_smem();
                 }
-                // rescaling O needs the previous tile's PV to be done
+                // rescaling O needs this head's previous PV to be done
                 if (rescale) {
-                    aborted = aborted ||
-                              !mbar_wait(&pv_done[(jj - 1) & 1], ((jj - 1) >> 1) & 1, abort_flag, fault);
+                    aborted = aborted || !mbar_wait(&pv_done[w], (jj - 1) & 1, abort_flag, fault);
                     if (!aborted) {
                         tc_fence_after();
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             uint32_t v[32];
-                            tmem_ld_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                            tmem_ld_32x32b_x32(ocol + c * 32, v);
                             tmem_wait_ld();
 #pragma unroll
                             for (int i = 0; i < 32; ++i)
                                 v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                            tmem_st_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                            tmem_st_32x32b_x32(ocol + c * 32, v);
                         }
                     }
                 }
-                // P = exp2(s - m) over S's own columns: high half 0-63, low 64-127
+                // pass 2: P = exp2(s - m) chunk by chunk into the chunk's own columns
                 float lsum = 0.f;
-                const uint32_t pcol = tmem + kColS + sb * 128 + lane_off;
+#pragma unroll 2
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t v[32];
+                    if (!aborted) {
+                        tmem_ld_32x32b_x32(scol + c * 32, v);
+                        tmem_wait_ld();
+                    } else {
 #pragma unroll
-                for (int grp = 0; grp < 4; ++grp) {
+                        for (int i = 0; i < 32; ++i) v[i] = 0u;
+                    }
                     uint32_t hi[16], lo[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float e0 = ex2_approx(s[grp * 32 + 2 * i] - m_run);
-                        const float e1 = ex2_approx(s[grp * 32 + 2 * i + 1] - m_run);
+                        const int kk = k0 + c * 32 + 2 * i;
+                        const float e0 = (masked && kk >= limit)
+                            ? 0.f : ex2_approx(fmaf(__uint_as_float(v[2 * i]), a.scale_log2, -m_run));
+                        const float e1 = (masked && kk + 1 >= limit)
+                            ? 0.f : ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), a.scale_log2, -m_run));
                         hi[i] = pack2<T>(e0, e1);
                         const float2 hv = unpack2<T>(hi[i]);
                         lo[i] = pack2<T>(e0 - hv.x, e1 - hv.y);
-                        lsum += I.precise ? e0 + e1 : hv.x + hv.y;
+                        lsum += e0 + e1;
                     }
                     if (!aborted) {
-                        tmem_st_32x32b_x16(pcol + grp * 16, hi);
-                        if (I.precise) tmem_st_32x32b_x16(pcol + 64 + grp * 16, lo);
+                        tmem_st_32x32b_x16(scol + c * 32, hi);
+                        tmem_st_32x32b_x16(scol + c * 32 + 16, lo);
                     }
                 }
                 l += lsum;
@@ -474,26 +531,21 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     tmem_wait_st();
                     tc_fence_before();
                 }
-                mbar_arrive(p_full);
+                mbar_arrive(&p_full[w]);
             }
-            // ---- O / l for this item's rows ----
-            aborted = aborted ||
-                      !mbar_wait(&pv_done[(jj - 1) & 1], ((jj - 1) >> 1) & 1, abort_flag, fault);
+            // ---- O / l for this head's rows ----
+            aborted = aborted || !mbar_wait(&pv_done[w], (jj - 1) & 1, abort_flag, fault);
             if (!aborted) {
                 tc_fence_after();
                 const float inv = l > 0.f ? 1.f / l : 0.f;
                 OT *orow = static_cast<OT *>(a.out) +
-                           ((int64_t)(I.q0 + r) * a.q_heads + I.h) * 128;
+                           ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem + kColO + c * 32 + lane_off, v);
+                    tmem_ld_32x32b_x32(ocol + c * 32, v);
                     tmem_wait_ld();
-                    if (row_ok) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            orow[c * 32 + i] = from_f32<OT>(__uint_as_float(v[i]) * inv);
-                    }
+                    if (row_ok) store_row32<OT>(orow + c * 32, v, inv);
                 }
                 tc_fence_before();
             }
@@ -637,6 +689,7 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
     args.block_count = (uint32_t)layer->block_count;
     args.scale_log2 = scale * pkv::kLog2e;
     args.causal = causal;
+    args.paired = ((q_heads / kvh) % 2) == 0;
     const cudaStream_t s = (cudaStream_t)stream;
     int ok = 1;
     for (size_t b0 = 0; ok && b0 < batch->batch; b0 += pkv::kPfMaxBatch) {
