@@ -156,6 +156,41 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// Three-input max (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed two-lane FP32 arithmetic (sm_100 .f32x2): one instruction per pair.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("{\n.reg .b64 ra, rb, rc;\nmov.b64 ra, {%1, %2};\nmov.b64 rb, {%3, %4};\n"
+        "mov.b64 rc, {%5, %6};\nfma.rn.f32x2 %0, ra, rb, rc;\n}"
+        : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+    return r;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    uint64_t d;
+    asm("{\n.reg .b64 ra, rb;\nmov.b64 ra, {%1, %2};\nmov.b64 rb, {%3, %4};\n"
+        "add.rn.f32x2 %0, ra, rb;\n}"
+        : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+    return r;
+}
+
+// Scores of keys at or past `limit` in the 32-key chunk starting at key kc
+// become -inf (their weight is exactly 0).
+__device__ __forceinline__ void mask_chunk(uint32_t (&v)[32], int kc, int limit) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        if (kc + i >= limit) v[i] = 0xff800000u;
+}
+
 template <typename T>
 struct Bf16Flag { static constexpr bool value = false; };
 template <>
@@ -449,11 +484,10 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = 0u;
                     }
+                    if (masked) mask_chunk(v, k0 + c * 32, limit);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const bool dead = masked && k0 + c * 32 + i >= limit;
-                        mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(v[i]));
-                    }
+                    for (int i = 0; i < 16; ++i)
+                        mx = max3(mx, __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
                 }
                 mx *= a.scale_log2;  // scale > 0 commutes with max
                 float alpha = 1.f;
@@ -496,8 +530,12 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                         }
                     }
                 }
-                // pass 2: P = exp2(s - m) chunk by chunk into the chunk's own columns
-                float lsum = 0.f;
+                // pass 2: P = exp2(s * scale - m) chunk by chunk into the chunk's
+                // own columns, as a 16-bit high half and the low remainder
+                const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+                const float2 nm2 = make_float2(-m_run, -m_run);
+                const float2 neg1 = make_float2(-1.f, -1.f);
+                float2 lsum2 = make_float2(0.f, 0.f);
 #pragma unroll 2
                 for (int c = 0; c < 4; ++c) {
                     uint32_t v[32];
@@ -508,24 +546,25 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = 0u;
                     }
+                    if (masked) mask_chunk(v, k0 + c * 32, limit);
                     uint32_t hi[16], lo[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int kk = k0 + c * 32 + 2 * i;
-                        const float e0 = (masked && kk >= limit)
-                            ? 0.f : ex2_approx(fmaf(__uint_as_float(v[2 * i]), a.scale_log2, -m_run));
-                        const float e1 = (masked && kk + 1 >= limit)
-                            ? 0.f : ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), a.scale_log2, -m_run));
-                        hi[i] = pack2<T>(e0, e1);
-                        const float2 hv = unpack2<T>(hi[i]);
-                        lo[i] = pack2<T>(e0 - hv.x, e1 - hv.y);
-                        lsum += e0 + e1;
+                        const float2 x = ffma2(
+                            make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                            sc2, nm2);
+                        const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        hi[i] = pack2<T>(e.x, e.y);
+                        const float2 rem = ffma2(unpack2<T>(hi[i]), neg1, e);  // exact
+                        lo[i] = pack2<T>(rem.x, rem.y);
+                        lsum2 = fadd2(lsum2, e);
                     }
                     if (!aborted) {
                         tmem_st_32x32b_x16(scol + c * 32, hi);
                         tmem_st_32x32b_x16(scol + c * 32 + 16, lo);
                     }
                 }
+                const float lsum = lsum2.x + lsum2.y;
                 l += lsum;
                 if (!aborted) {
                     tmem_wait_st();
