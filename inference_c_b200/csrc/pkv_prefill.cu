@@ -55,6 +55,8 @@ constexpr uint32_t kBarOff = kVOff + kStages * 32768;
 constexpr uint32_t kMiscOff = kBarOff + 256;
 constexpr uint32_t kPrefixOff = kMiscOff + 256;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kRegsControl = 64, kRegsSoftmax = 216;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kPfThreads * 168, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 
 size_t pf_smem_bytes(int batch) { return kPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
@@ -299,6 +301,10 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
     const int64_t total_items = prefix[a.batch];
     uint32_t *fault = &g_prefill_fault;
 
+    if (warp < 4) {
+    // Control warpgroup (producer, MMA issuer, two idle warps) hands registers
+    // to the softmax warpgroups: 128 x 64 + 256 x 216 = 384 x 168.
+    setmaxnreg_dec<kRegsControl>();
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
         uint32_t jj = 0, qi = 0;
@@ -449,17 +455,23 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             }
         }
         __syncwarp();
-    } else if (warp >= 4 && (warp < 8 || paired)) {
+    }
+    } else if (warp < 8 || paired) {
+        setmaxnreg_inc<kRegsSoftmax>();
         // ------------------------------- softmax -------------------------------
-        // Same loops and the same waits on an abort, minus the TMEM traffic.
+        // A wait that gives up (abort or timeout) ends the warp's work; the
+        // vote keeps the .sync.aligned TMEM instructions warp-uniform.
+        auto wait = [&](uint64_t *bar, uint32_t par) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(bar, par, abort_flag, fault));
+        };
         const int w = warp < 8 ? 0 : 1;         // head A or head B
         const int q4 = warp & 3;
         const int r = q4 * 32 + lane;            // query row = TMEM lane
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
         const uint32_t ocol = tmem + w * 256 + 128 + lane_off;
         uint32_t jj = 0;
-        bool aborted = false;
-        for (int64_t u = blockIdx.x; u < total_items; u += gridDim.x) {
+        bool ok = true;
+        for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
             const Item I = item_at(u, prefix, a);
             if (I.bad || I.ntiles == 0) continue;
             const bool row_ok = r < I.nrows;
@@ -470,25 +482,23 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 const int k0 = jt * kPfTile;
                 const bool masked = k0 + kPfTile > limit;
                 const uint32_t scol = tmem + (paired ? (uint32_t)w : (jj & 1u)) * 256u + lane_off;
-                aborted = aborted || !mbar_wait(&s_full[w], jj & 1, abort_flag, fault);
-                if (!aborted) tc_fence_after();
-                // pass 1: row max
+                if (!wait(&s_full[w], jj & 1)) { ok = false; break; }
+                tc_fence_after();
+                // the row's 128 scores in registers with one TMEM round trip
+                uint32_t v[4][32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(scol + c * 32, v[c]);
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) mask_chunk(v[c], k0 + c * 32, limit);
+                }
                 float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t v[32];
-                    if (!aborted) {
-                        tmem_ld_32x32b_x32(scol + c * 32, v);
-                        tmem_wait_ld();
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = 0u;
-                    }
-                    if (masked) mask_chunk(v, k0 + c * 32, limit);
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
                     for (int i = 0; i < 16; ++i)
-                        mx = max3(mx, __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-                }
+                        mx = max3(mx, __uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]));
                 mx *= a.scale_log2;  // scale > 0 commutes with max
                 float alpha = 1.f;
                 bool rescale = false;
@@ -502,7 +512,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 // zeroes them (once their TMA landed) before either PV reads.
                 if (w == 0 && k0 + kPfTile > I.L) {
                     const int st = (int)(jj % kStages);
-                    aborted = aborted || !mbar_wait(&vfull[st], (jj / kStages) & 1, abort_flag, fault);
+                    if (!wait(&vfull[st], (jj / kStages) & 1)) { ok = false; break; }
                     if (k0 + r >= I.L) {
                         unsigned char *vrow = sm + kVOff + st * 32768 + r * 128;
 #pragma unroll
@@ -514,80 +524,64 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     fence_proxy_async_smem();
                 }
                 // rescaling O needs this head's previous PV to be done
-                if (rescale) {
-                    aborted = aborted || !mbar_wait(&pv_done[w], (jj - 1) & 1, abort_flag, fault);
-                    if (!aborted) {
-                        tc_fence_after();
+                if (__any_sync(0xffffffffu, rescale)) {
+                    if (!wait(&pv_done[w], (jj - 1) & 1)) { ok = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t v[32];
-                            tmem_ld_32x32b_x32(ocol + c * 32, v);
-                            tmem_wait_ld();
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(ocol + c * 32, o);
+                        tmem_wait_ld();
 #pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                            tmem_st_32x32b_x32(ocol + c * 32, v);
-                        }
+                        for (int i = 0; i < 32; ++i)
+                            o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st_32x32b_x32(ocol + c * 32, o);
                     }
                 }
-                // pass 2: P = exp2(s * scale - m) chunk by chunk into the chunk's
-                // own columns, as a 16-bit high half and the low remainder
+                // P = exp2(s * scale - m) chunk by chunk into the chunk's own
+                // columns, as a 16-bit high half and the low remainder
                 const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
                 const float2 nm2 = make_float2(-m_run, -m_run);
                 const float2 neg1 = make_float2(-1.f, -1.f);
                 float2 lsum2 = make_float2(0.f, 0.f);
-#pragma unroll 2
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t v[32];
-                    if (!aborted) {
-                        tmem_ld_32x32b_x32(scol + c * 32, v);
-                        tmem_wait_ld();
-                    } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = 0u;
-                    }
-                    if (masked) mask_chunk(v, k0 + c * 32, limit);
+                for (int c = 0; c < 4; ++c) {
                     uint32_t hi[16], lo[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float2 x = ffma2(
-                            make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
-                            sc2, nm2);
+                        const float2 x = ffma2(make_float2(__uint_as_float(v[c][2 * i]),
+                                                           __uint_as_float(v[c][2 * i + 1])),
+                                               sc2, nm2);
                         const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
                         hi[i] = pack2<T>(e.x, e.y);
                         const float2 rem = ffma2(unpack2<T>(hi[i]), neg1, e);  // exact
                         lo[i] = pack2<T>(rem.x, rem.y);
                         lsum2 = fadd2(lsum2, e);
                     }
-                    if (!aborted) {
-                        tmem_st_32x32b_x16(scol + c * 32, hi);
-                        tmem_st_32x32b_x16(scol + c * 32 + 16, lo);
-                    }
+                    tmem_st_32x32b_x16(scol + c * 32, hi);
+                    tmem_st_32x32b_x16(scol + c * 32 + 16, lo);
                 }
-                const float lsum = lsum2.x + lsum2.y;
-                l += lsum;
-                if (!aborted) {
-                    tmem_wait_st();
-                    tc_fence_before();
-                }
+                l += lsum2.x + lsum2.y;
+                tmem_wait_st();
+                tc_fence_before();
                 mbar_arrive(&p_full[w]);
             }
             // ---- O / l for this head's rows ----
-            aborted = aborted || !mbar_wait(&pv_done[w], (jj - 1) & 1, abort_flag, fault);
-            if (!aborted) {
-                tc_fence_after();
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                OT *orow = static_cast<OT *>(a.out) +
-                           ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(ocol + c * 32, v);
-                    tmem_wait_ld();
-                    if (row_ok) store_row32<OT>(orow + c * 32, v, inv);
-                }
-                tc_fence_before();
+            if (!ok || !wait(&pv_done[w], (jj - 1) & 1)) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            OT *orow = static_cast<OT *>(a.out) + ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld_32x32b_x32(ocol + c * 32, o);
+                tmem_wait_ld();
+                if (row_ok) store_row32<OT>(orow + c * 32, o, inv);
+            }
+            tc_fence_before();
         }
     }
     tc_fence_before();
