@@ -33,6 +33,8 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
 #include "pkv_sm100.cuh"
@@ -245,6 +247,31 @@ __device__ __forceinline__ void store_row32(OT *dst, const uint32_t (&v)[32], fl
     }
 }
 
+// S[128 q][128 k] = Q . K^T: eight K=16 steps over the two 64-column halves
+// of Q and K (SWIZZLE_128B, K-major: step kk starts 32 bytes further along a
+// 128-byte row; steps 4-7 read the second half).
+__host__ __device__ constexpr uint32_t s_step(uint32_t kk) { return ((kk >> 2) * kHalf + (kk & 3) * 32) >> 4; }
+__host__ __device__ constexpr uint32_t p_col(uint32_t kk) { return (kk >> 1) * 32 + (kk & 1) * 8; }
+__host__ __device__ constexpr uint32_t v_step(uint32_t kk) { return kk * (2048 >> 4); }
+
+template <uint32_t... KK>
+__device__ __forceinline__ void s_mmas(uint32_t dst, uint64_t qd, uint64_t kd, uint32_t idesc,
+                                       std::integer_sequence<uint32_t, KK...>) {
+    (sm100::mma_f16_ss_at<s_step(KK), s_step(KK)>(dst, qd, kd, idesc, KK > 0 ? 1u : 0u), ...);
+}
+// O[128 q][128 d] (+)= P . V with P from TMEM: step kk covers keys 16kk..16kk+15,
+// whose high halves sit in columns 32(kk/2) + 8(kk%2) .. +7 and low halves 16
+// columns further; V (MN-major) advances 16 rows = 2048 bytes per step.  The
+// high-half MMAs run first (the first of a sequence starts the accumulator),
+// then the low halves add in.
+template <uint32_t... KK>
+__device__ __forceinline__ void pv_mmas(uint32_t ocol, uint32_t pcol, uint64_t vd, uint32_t idesc,
+                                        uint32_t acc, std::integer_sequence<uint32_t, KK...>) {
+    (sm100::mma_f16_ts_at<p_col(KK), v_step(KK)>(ocol, pcol, vd, idesc, (acc | KK) ? 1u : 0u),
+     ...);
+    (sm100::mma_f16_ts_at<p_col(KK) + 16, v_step(KK)>(ocol, pcol, vd, idesc, 1u), ...);
+}
+
 template <typename T, typename OT>
 __global__ void __launch_bounds__(kPfThreads, 1)
 paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap,
@@ -384,50 +411,35 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             auto sbuf = [&](int w, uint32_t t) -> uint32_t {
                 return tmem + (paired ? (uint32_t)w : (t & 1u)) * 256u;
             };
-            // S of head w for global tile t.  Its S/P buffer is free once the
-            // PV that last read it completed: tile t-1 of the head (paired),
-            // tile t-2 (unpaired).
+            // S of head w for global tile t.  Its S/P buffer was last read by
+            // a PV MMA this thread issued earlier; tcgen05.mma operations of
+            // one thread execute in issue order, so the new S overwrites the
+            // old P only after that PV consumed it (the same ordering the
+            // CUTLASS sm100 FMHA mainloop relies on for its S/P aliasing).
+            // Shared-memory descriptors of the tiles; a k-step or a stage moves
+            // the start-address field (16-byte units, bits 0-13) by a constant.
+            const uint64_t qdesc = sw128_desc(smem_u32(sm + kQOff), 16, 1024);
+            const uint64_t kdesc = sw128_desc(smem_u32(sm + kKOff), 16, 1024);
+            const uint64_t vdesc = sw128_desc(smem_u32(sm + kVOff), kHalf, 1024);
             auto issue_s = [&](int w, uint32_t t) -> bool {
-                if (paired || t >= 2) {
-                    const uint32_t par = paired ? (t & 1) ^ 1 : (t & 1);
-                    if (!mbar_wait(&pv_done[w], par, abort_flag, fault)) return false;
-                }
-                tc_fence_after();
-                const uint32_t qaddr = smem_u32(sm + kQOff + w * 2 * kHalf);
-                const uint32_t kaddr = smem_u32(sm + kKOff + (t % kStages) * 32768);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t ad = sw128_desc(qaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-                    mma_f16_ss(sbuf(w, t), ad, bd, kIdescS, kk > 0);
-                }
+                const uint64_t qd = qdesc + (uint64_t)((uint32_t)w * (2 * kHalf >> 4));
+                const uint64_t kd = kdesc + (uint64_t)((t % kStages) * (32768u >> 4));
+                s_mmas(sbuf(w, t), qd, kd, kIdescS, std::make_integer_sequence<uint32_t, 8>{});
                 mma_commit(&s_full[w]);
                 return true;
             };
             // PV of head w for global tile t (jt: its index within the item),
             // then release the tile's V stage when no other head still reads it.
-            // P of 32-key chunk c: high half in columns 32c..32c+15, low half
-            // in 32c+16..32c+31 of the S/P buffer.
             auto issue_pv = [&](int w, uint32_t t, int jt, bool last_reader) -> bool {
                 const int st = (int)(t % kStages);
                 if (!mbar_wait(&vfull[st], (t / kStages) & 1, abort_flag, fault) ||
                     !mbar_wait(&p_full[w], t & 1, abort_flag, fault))
                     return false;
                 tc_fence_after();
-                const uint32_t vaddr = smem_u32(sm + kVOff + st * 32768);
-                const uint32_t pcol = sbuf(w, t);
+                const uint64_t vd = vdesc + (uint64_t)((uint32_t)st * (32768u >> 4));
                 const uint32_t ocol = tmem + (paired ? (uint32_t)w * 256u : 0u) + 128u;
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                    mma_f16_ts(ocol, pcol + (kk >> 1) * 32 + (kk & 1) * 8, bd, kIdescPV,
-                               (jt > 0 || kk > 0) ? 1u : 0u);
-                }
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t bd = sw128_desc(vaddr + kk * 2048, kHalf, 1024);
-                    mma_f16_ts(ocol, pcol + (kk >> 1) * 32 + 16 + (kk & 1) * 8, bd, kIdescPV, 1u);
-                }
+                pv_mmas(ocol, sbuf(w, t), vd, kIdescPV, jt > 0 ? 1u : 0u,
+                        std::make_integer_sequence<uint32_t, 8>{});
                 mma_commit(&pv_done[w]);
                 if (last_reader) mma_commit(&vempty[st]);
                 return true;
@@ -493,12 +505,17 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
 #pragma unroll
                     for (int c = 0; c < 4; ++c) mask_chunk(v[c], k0 + c * 32, limit);
                 }
-                float mx = -INFINITY;
+                float mc[4];  // one running max per chunk: four short chains
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 4; ++c) {
+                    mc[c] = max3(__uint_as_float(v[c][0]), __uint_as_float(v[c][1]),
+                                 __uint_as_float(v[c][2]));
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        mx = max3(mx, __uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]));
+                    for (int i = 3; i < 31; i += 2)
+                        mc[c] = max3(mc[c], __uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1]));
+                    mc[c] = fmaxf(mc[c], __uint_as_float(v[c][31]));
+                }
+                float mx = max3(mc[0], mc[1], fmaxf(mc[2], mc[3]));
                 mx *= a.scale_log2;  // scale > 0 commutes with max
                 float alpha = 1.f;
                 bool rescale = false;

@@ -141,6 +141,31 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// The same two MMAs with the k-step offsets (16-byte units) added to the
+// descriptors inside the asm block, so an unrolled issue loop keeps one base
+// descriptor per operand in registers instead of one per k-step.
+template <uint32_t AOFF, uint32_t BOFF>
+__device__ __forceinline__ void mma_f16_ss_at(uint32_t d_tmem, uint64_t a_base, uint64_t b_base,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+        "add.s64 ad, %1, %5;\n\tadd.s64 bd, %2, %6;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_base), "l"(b_base), "r"(idesc), "r"(accumulate), "n"(AOFF), "n"(BOFF)
+        : "memory");
+}
+template <uint32_t ACOL, uint32_t BOFF>
+__device__ __forceinline__ void mma_f16_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_base,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b32 at;\n\t.reg .b64 bd;\n\t"
+        "add.s32 at, %1, %5;\n\tadd.s64 bd, %2, %6;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [at], bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_base), "r"(idesc), "r"(accumulate), "n"(ACOL), "n"(BOFF)
+        : "memory");
+}
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
