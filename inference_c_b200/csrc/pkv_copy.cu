@@ -39,6 +39,7 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
                const int32_t *__restrict__ seq_lens, const int32_t *__restrict__ offsets,
                int batch, int32_t total_rows, int vec_per_row, int block_size,
                int block_shift, uint32_t block_count, bool tail) {
+    pdl_launch_dependents();  // a decode launched after this may set itself up now
     const int lane = threadIdx.x & 31;
     const int32_t row = blockIdx.x * kCopyWarps + (threadIdx.x >> 5);
     if (row >= total_rows) return;
@@ -99,6 +100,7 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
 
 __global__ void apply_patches_kernel(uint32_t *table, int64_t stride, int64_t rows,
                                      const PkvTablePatch *patches, int64_t count) {
+    pdl_launch_dependents();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const PkvTablePatch p = patches[i];

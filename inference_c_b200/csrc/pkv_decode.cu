@@ -458,7 +458,7 @@ constexpr uint32_t kTcPOff = kTcQOff + 2 * 4096;
 constexpr uint32_t kTcPBuf = 8192;        // one P^T tile of up to 32 rows
 constexpr uint32_t kTcBarOff = kTcPOff + 2 * kTcPBuf;
 constexpr uint32_t kTcMiscOff = kTcBarOff + 256;
-constexpr uint32_t kTcPrefixOff = kTcMiscOff + 2048;
+constexpr uint32_t kTcPrefixOff = kTcMiscOff + 4096;
 constexpr uint32_t kTcTmemCols = 128;
 
 size_t tc_smem_bytes(int batch) { return kTcPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
@@ -568,61 +568,95 @@ struct IsBf16 { static constexpr bool value = false; };
 template <>
 struct IsBf16<__nv_bfloat16> { static constexpr bool value = true; };
 
-// Merges the partials of head h of segment (b, g): m/l of every piece are
-// staged in shared memory (`stage`, 3 floats per piece), then each thread
-// sums its output element over the pieces.  `tid`/`nthr` are the
-// participating threads; `sync` is their barrier.
+// Merges the partials of heads [h0, h0 + nh) of segment (b, g) into `out`
+// (nh rows of 128).  Every piece's max per head is staged in shared memory
+// (`wst`, np * nh floats), one thread per head turns them into weights
+// exp2(m_c - m) / l over the pieces, then each output float4 is the weighted
+// sum of the pieces' partial rows: `ps` threads share one float4 (pieces
+// c = lane-in-share mod ps, summed through `red`, ps * nh * 32 float4s), each
+// keeping up to 8 loads in flight.  `tid`/`nthr` are the participating
+// threads; `sync` is their barrier.
 template <typename OT, typename Sync>
-__device__ __forceinline__ void merge_head(const TcArgs &a, int h, int64_t seg, int nt, int ncta,
-                                           int64_t T, int tid, int nthr, float *stage, int cap,
-                                           OT *outh, Sync sync) {
+__device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, int64_t seg, int nt,
+                                              int ncta, int64_t T, int tid, int nthr, int ps,
+                                              float *wst, int *slot, float4 *red, int cap,
+                                              OT *out, Sync sync) {
     const int first = cta_of_tile(seg, ncta, T);
     const int np = cta_of_tile(seg + nt - 1, ncta, T) - first + 1;
     if (np > cap) {  // cannot happen with the host's choice of merge mode
         if (tid == 0) record_fault(&g_decode_fault, kFaultPositionOutOfRange);
         return;
     }
-    for (int c = tid; c < np; c += nthr) {
-        const int cta = first + c;
-        const int k = piece_slot(cta, seg, ncta, T);
-        const float *ml = a.part_ml + (((int64_t)cta * 2 + k) * 16 + h) * 2;
-        stage[3 * c] = __ldcg(ml);
-        stage[3 * c + 1] = __ldcg(ml + 1);
-        stage[3 * c + 2] = __int_as_float(k);
+    for (int c = tid; c < np; c += nthr) slot[c] = piece_slot(first + c, seg, ncta, T);
+    sync();
+    for (int i = tid; i < np * nh; i += nthr) {
+        const int c = i / nh, h = h0 + (i - c * nh);
+        wst[i] = __ldcg(a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h) * 2);
     }
     sync();
-    float mx = -INFINITY;
-    for (int c = 0; c < np; ++c) mx = fmaxf(mx, stage[3 * c]);
-    float lt = 0.f, ot = 0.f;
-    for (int d = tid; d < 128; d += nthr) {
-        lt = 0.f;
-        ot = 0.f;
-        int c = 0;
-        for (; c + 4 <= np; c += 4) {  // four independent loads in flight
-            float v[4], f[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int cta = first + c + i;
-                const int k = __float_as_int(stage[3 * (c + i) + 2]);
-                v[i] = __ldcg(a.part_o + (((int64_t)cta * 2 + k) * 16 + h) * 128 + d);
-                const float mc = stage[3 * (c + i)];
-                f[i] = mc == -INFINITY ? 0.f : exp2f(mc - mx);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                lt += stage[3 * (c + i) + 1] * f[i];
-                ot += v[i] * f[i];
-            }
-        }
-        for (; c < np; ++c) {
-            const int cta = first + c;
-            const int k = __float_as_int(stage[3 * c + 2]);
-            const float mc = stage[3 * c];
+    for (int hh = tid; hh < nh; hh += nthr) {
+        float mx = -INFINITY;
+        for (int c = 0; c < np; ++c) mx = fmaxf(mx, wst[c * nh + hh]);
+        float lt = 0.f;
+        for (int c = 0; c < np; ++c) {
+            const float mc = wst[c * nh + hh];
             const float f = mc == -INFINITY ? 0.f : exp2f(mc - mx);
-            lt += stage[3 * c + 1] * f;
-            ot += __ldcg(a.part_o + (((int64_t)cta * 2 + k) * 16 + h) * 128 + d) * f;
+            lt += __ldcg(a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h0 + hh) * 2 + 1) * f;
+            wst[c * nh + hh] = f;
         }
-        outh[d] = from_f32<OT>(lt > 0.f ? ot / lt : 0.f);
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        for (int c = 0; c < np; ++c) wst[c * nh + hh] *= inv;
+    }
+    sync();
+    const int nf = nh * 32;  // float4s of output
+    for (int base = 0; base < nf * ps; base += nthr) {
+        const int w = base + tid;
+        const int f4 = w % nf, pl = w / nf;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (pl < ps) {
+            const int hh = f4 >> 5, d = (f4 & 31) * 4;
+            for (int c0 = pl; c0 < np; c0 += 8 * ps) {
+                float4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = c0 + i * ps;
+                    v[i] = c < np ? __ldcg(reinterpret_cast<const float4 *>(
+                                        a.part_o + (((int64_t)(first + c) * 2 + slot[c]) * 16 +
+                                                    h0 + hh) * 128 + d))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int c = c0 + i * ps;
+                    const float f = c < np ? wst[c * nh + hh] : 0.f;
+                    acc.x += f * v[i].x;
+                    acc.y += f * v[i].y;
+                    acc.z += f * v[i].z;
+                    acc.w += f * v[i].w;
+                }
+            }
+        }
+        if (ps > 1) {
+            if (pl < ps) red[w] = acc;
+            sync();
+            if (pl == 0) {
+                for (int k = 1; k < ps; ++k) {
+                    const float4 r = red[k * nf + f4];
+                    acc.x += r.x;
+                    acc.y += r.y;
+                    acc.z += r.z;
+                    acc.w += r.w;
+                }
+            }
+        }
+        if (pl == 0) {
+            OT *o = out + (f4 >> 5) * 128 + (f4 & 31) * 4;
+            o[0] = from_f32<OT>(acc.x);
+            o[1] = from_f32<OT>(acc.y);
+            o[2] = from_f32<OT>(acc.z);
+            o[3] = from_f32<OT>(acc.w);
+        }
+        if (ps > 1) sync();
     }
     sync();
 }
@@ -651,7 +685,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     int *scan = reinterpret_cast<int *>(sm + kTcMiscOff + 32);    // 8 ints
     float *red = reinterpret_cast<float *>(sm + kTcMiscOff + 64);  // [2][4][16]
     float *lred = red + 128;                                        // [4][16]
-    float *mstage = lred + 64;                                      // 3 * kInKernelMergeMax
+    float *mwst = lred + 64;                                        // kInKernelMergeMax * 16
+    int *mslot = reinterpret_cast<int *>(mwst + kInKernelMergeMax * 16);  // kInKernelMergeMax
     int *prefix = reinterpret_cast<int *>(sm + kTcPrefixOff);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -683,6 +718,11 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         tma_prefetch_desc(&kmap);
         tma_prefetch_desc(&vmap);
     }
+    // Everything above touches only this CTA's shared memory and TMEM, so it
+    // overlaps the previous kernel under programmatic dependent launch; from
+    // here on global memory written by earlier kernels (pages, tables,
+    // lengths, queries) is read.
+    pdl_wait();
     build_tile_prefix(a, prefix, scan);
     fence_proxy_async_smem();
     tc_fence_before();
@@ -936,10 +976,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             group_sync();
             if (*ticket) {
                 __threadfence();
-#pragma unroll 1
-                for (int h = 0; h < G; ++h)
-                    merge_head<OT>(a, h, P.seg, P.nt, ncta, total_tiles, wt, 128, mstage,
-                                   kInKernelMergeMax, out + h * 128, group_sync);
+                merge_segment<OT>(a, 0, G, P.seg, P.nt, ncta, total_tiles, wt, 128, 1, mwst,
+                                  mslot, nullptr, kInKernelMergeMax, out, group_sync);
                 if (wt == 0) a.counters[(int64_t)P.b * a.kv_heads + P.g] = 0u;
             }
         }
@@ -957,11 +995,15 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
 }
 
 // Merges segments that span more than kInKernelMergeMax CTAs.  Grid:
-// (kv_heads * G, batch); block: 128 threads, one output element each.
+// (kv_heads * G, batch), one query head per CTA; 128 threads, four per output
+// float4 (each summing every fourth piece).
 template <typename OT>
 __global__ void __launch_bounds__(128)
 pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
-    __shared__ float stage[3 * kTcMaxGrid];
+    pdl_wait();
+    __shared__ float wst[kTcMaxGrid];
+    __shared__ int slot[kTcMaxGrid];
+    __shared__ float4 red[128];
     const int b = blockIdx.y;
     const int g = blockIdx.x / group, h = blockIdx.x - g * group;
     const int64_t T = a.tile_prefix[a.batch];
@@ -972,8 +1014,8 @@ pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     if (cta_of_tile(seg, ncta, T) == cta_of_tile(seg + nt - 1, ncta, T)) return;
     OT *out = static_cast<OT *>(a.out) +
               ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) * 128;
-    merge_head<OT>(a, h, seg, nt, ncta, T, threadIdx.x, 128, stage, kTcMaxGrid, out,
-                   [] { __syncthreads(); });
+    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, 128, 4, wst, slot, red, kTcMaxGrid,
+                      out, [] { __syncthreads(); });
 }
 
 int g_sm_count[64];
@@ -1080,10 +1122,29 @@ int launch_tc(const TcArgs &args, const CUtensorMap &km, const CUtensorMap &vm, 
             return 0;
         configured[dev] = 1;
     }
-    kern<<<ncta, kTcThreads, tc_smem_bytes(args.batch), stream>>>(args, km, vm);
-    if (!args.merge_in_kernel)
-        pkv_tc_merge_kernel<OT><<<dim3(args.kv_heads * G, args.batch), 128, 0, stream>>>(args, G,
-                                                                                         ncta);
+    // Programmatic dependent launch: the prologue (barriers, TMEM, shared
+    // memory) overlaps the tail of the kernel before it in the stream.  The
+    // decode kernel itself never releases its dependents early: a merge CTA
+    // waiting on an SM could keep a decode CTA from being placed.
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ncta);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = tc_smem_bytes(args.batch);
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, args, km, vm) != cudaSuccess) return 0;
+    if (!args.merge_in_kernel) {
+        cudaLaunchConfig_t mc = cfg;
+        mc.gridDim = dim3(args.kv_heads * G, args.batch);
+        mc.blockDim = dim3(128);
+        mc.dynamicSmemBytes = 0;
+        if (cudaLaunchKernelEx(&mc, pkv_tc_merge_kernel<OT>, args, G, ncta) != cudaSuccess)
+            return 0;
+    }
     return cudaGetLastError() == cudaSuccess;
 }
 

@@ -72,6 +72,16 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
     return __float2bfloat16_rn(v);
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel of
+// the stream (when launched with programmatic serialization) start its
+// prologue while this one runs; wait blocks until every kernel this one
+// depends on has finished and its writes are visible.  Both are no-ops for
+// kernels launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
