@@ -458,10 +458,13 @@ constexpr uint32_t kTcPOff = kTcQOff + 2 * 4096;
 constexpr uint32_t kTcPBuf = 8192;        // one P^T tile of up to 32 rows
 constexpr uint32_t kTcBarOff = kTcPOff + 2 * kTcPBuf;
 constexpr uint32_t kTcMiscOff = kTcBarOff + 256;
-constexpr uint32_t kTcPrefixOff = kTcMiscOff + 4096;
+constexpr uint32_t kTcPrefixOff = kTcMiscOff + 5120;
 constexpr uint32_t kTcTmemCols = 128;
 
 size_t tc_smem_bytes(int batch) { return kTcPrefixOff + 4u * ((size_t)batch + 1u) + 1024u; }
+static_assert(kTcPrefixOff + 4u * (kTcMaxBatch + 1u) + 1024u <= 232448u, "shared memory budget");
+static_assert(64 + 512 + 256 + 2 * 4 * 16 * kInKernelMergeMax + 4 * kInKernelMergeMax <= 5120,
+              "misc area");
 
 struct TcArgs {
     const uint32_t *tables;
@@ -569,18 +572,18 @@ template <>
 struct IsBf16<__nv_bfloat16> { static constexpr bool value = true; };
 
 // Merges the partials of heads [h0, h0 + nh) of segment (b, g) into `out`
-// (nh rows of 128).  Every piece's max per head is staged in shared memory
-// (`wst`, np * nh floats), one thread per head turns them into weights
-// exp2(m_c - m) / l over the pieces, then each output float4 is the weighted
-// sum of the pieces' partial rows: `ps` threads share one float4 (pieces
-// c = lane-in-share mod ps, summed through `red`, ps * nh * 32 float4s), each
-// keeping up to 8 loads in flight.  `tid`/`nthr` are the participating
-// threads; `sync` is their barrier.
+// (nh rows of 128).  Every piece's (m, l) per head is staged in shared memory
+// (`wst`, `lst`: np * nh floats each); one warp per head, lanes over the
+// pieces, turns them into weights exp2(m_c - m) / l; then each output float4
+// is the weighted sum of the pieces' partial rows: `ps` threads share one
+// float4 (pieces c = lane-in-share mod ps, summed through `red`,
+// ps * nh * 32 float4s), each keeping up to 16 loads in flight.  `tid`/`nthr`
+// are the participating threads (whole warps); `sync` is their barrier.
 template <typename OT, typename Sync>
 __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, int64_t seg, int nt,
                                               int ncta, int64_t T, int tid, int nthr, int ps,
-                                              float *wst, int *slot, float4 *red, int cap,
-                                              OT *out, Sync sync) {
+                                              float *wst, float *lst, int *slot, float4 *red,
+                                              int cap, OT *out, Sync sync) {
     const int first = cta_of_tile(seg, ncta, T);
     const int np = cta_of_tile(seg + nt - 1, ncta, T) - first + 1;
     if (np > cap) {  // cannot happen with the host's choice of merge mode
@@ -591,21 +594,28 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
     sync();
     for (int i = tid; i < np * nh; i += nthr) {
         const int c = i / nh, h = h0 + (i - c * nh);
-        wst[i] = __ldcg(a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h) * 2);
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(
+            a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h) * 2));
+        wst[i] = ml.x;
+        lst[i] = ml.y;
     }
     sync();
-    for (int hh = tid; hh < nh; hh += nthr) {
+    // weights: one warp per head, lanes over the pieces
+    for (int hh = tid >> 5; hh < nh; hh += nthr >> 5) {
+        const int lane = tid & 31;
         float mx = -INFINITY;
-        for (int c = 0; c < np; ++c) mx = fmaxf(mx, wst[c * nh + hh]);
+        for (int c = lane; c < np; c += 32) mx = fmaxf(mx, wst[c * nh + hh]);
+        mx = warp_max(mx);
         float lt = 0.f;
-        for (int c = 0; c < np; ++c) {
+        for (int c = lane; c < np; c += 32) {
             const float mc = wst[c * nh + hh];
             const float f = mc == -INFINITY ? 0.f : exp2f(mc - mx);
-            lt += __ldcg(a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h0 + hh) * 2 + 1) * f;
+            lt += lst[c * nh + hh] * f;
             wst[c * nh + hh] = f;
         }
+        lt = warp_sum(lt);
         const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        for (int c = 0; c < np; ++c) wst[c * nh + hh] *= inv;
+        for (int c = lane; c < np; c += 32) wst[c * nh + hh] *= inv;
     }
     sync();
     const int nf = nh * 32;  // float4s of output
@@ -615,10 +625,10 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (pl < ps) {
             const int hh = f4 >> 5, d = (f4 & 31) * 4;
-            for (int c0 = pl; c0 < np; c0 += 8 * ps) {
-                float4 v[8];
+            for (int c0 = pl; c0 < np; c0 += 16 * ps) {
+                float4 v[16];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 16; ++i) {
                     const int c = c0 + i * ps;
                     v[i] = c < np ? __ldcg(reinterpret_cast<const float4 *>(
                                         a.part_o + (((int64_t)(first + c) * 2 + slot[c]) * 16 +
@@ -626,7 +636,7 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 16; ++i) {
                     const int c = c0 + i * ps;
                     const float f = c < np ? wst[c * nh + hh] : 0.f;
                     acc.x += f * v[i].x;
@@ -686,7 +696,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     float *red = reinterpret_cast<float *>(sm + kTcMiscOff + 64);  // [2][4][16]
     float *lred = red + 128;                                        // [4][16]
     float *mwst = lred + 64;                                        // kInKernelMergeMax * 16
-    int *mslot = reinterpret_cast<int *>(mwst + kInKernelMergeMax * 16);  // kInKernelMergeMax
+    float *mlst = mwst + kInKernelMergeMax * 16;                    // kInKernelMergeMax * 16
+    int *mslot = reinterpret_cast<int *>(mlst + kInKernelMergeMax * 16);  // kInKernelMergeMax
     int *prefix = reinterpret_cast<int *>(sm + kTcPrefixOff);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -809,6 +820,29 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 t += P.k1 - P.k0;
                 if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag, fault)) break;
                 const uint32_t qaddr = smem_u32(sm + kTcQOff + (qi & 1) * 4096);
+                // PV of tile jp: O^T[buf] = V^T . P^T once the group wrote P
+                // and read the O of tile jp - 2 out of that buffer.
+                auto issue_pv = [&](uint32_t jp) -> bool {
+                    const int stage = (int)(jp % kTcStages);
+                    const uint32_t buf = jp & 1, par = (jp >> 1) & 1;
+                    if (!mbar_wait(&p_full[buf], par, abort_flag, fault) ||
+                        !mbar_wait(&o_empty[buf], par ^ 1, abort_flag, fault))
+                        return false;
+                    tc_fence_after();
+                    const uint32_t vaddr = smem_u32(sm + stage * kTcStageBytes) + 2 * kTcHalf;
+                    const uint32_t paddr = smem_u32(sm + kTcPOff + buf * kTcPBuf);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t ad = sw128_desc(vaddr + kk * 2048, kTcHalf, 1024);
+                        const uint64_t bd = sw128_desc(paddr + (kk >> 2) * kPChunk + (kk & 3) * 32, 16, 1024);
+                        mma_f16_ss(tmem + 32 + buf * PN, ad, bd, kIdescPV, kk > 0);
+                    }
+                    mma_commit(&o_full[buf]);
+                    mma_commit(&empty[stage]);
+                    return true;
+                };
+                // S of tile j is issued before the PV of tile j - 1, so the
+                // group finds the next scores ready when it finishes a tile.
                 for (int k = P.k0; k < P.k1; ++k, ++j) {
                     const int stage = (int)(j % kTcStages);
                     const uint32_t buf = j & 1, par = (j >> 1) & 1;
@@ -827,23 +861,12 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                     }
                     mma_commit(&s_full[buf]);
                     if (k == P.k1 - 1) mma_commit(&q_empty[qi & 1]);
-                    if (!mbar_wait(&p_full[buf], par, abort_flag, fault) ||
-                        !mbar_wait(&o_empty[buf], par ^ 1, abort_flag, fault)) {
+                    if (k > P.k0 && !issue_pv(j - 1)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t vaddr = kaddr + 2 * kTcHalf;
-                    const uint32_t paddr = smem_u32(sm + kTcPOff + buf * kTcPBuf);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t ad = sw128_desc(vaddr + kk * 2048, kTcHalf, 1024);
-                        const uint64_t bd = sw128_desc(paddr + (kk >> 2) * kPChunk + (kk & 3) * 32, 16, 1024);
-                        mma_f16_ss(tmem + 32 + buf * PN, ad, bd, kIdescPV, kk > 0);
-                    }
-                    mma_commit(&o_full[buf]);
-                    mma_commit(&empty[stage]);
                 }
+                if (ok && P.k1 > P.k0 && !issue_pv(j - 1)) ok = false;
                 ++qi;
             }
         }
@@ -872,9 +895,32 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 l_part[h] = 0.f;
                 acc[h] = 0.f;
             }
+            // O of tile jp (its PV used P relative to the max of tile jp) folds
+            // into acc after the correction alpha of tile jp.
+            float alpha_prev[G];
+            auto fold = [&](uint32_t jp) {
+                const uint32_t buf = jp & 1, par = (jp >> 1) & 1;
+                aborted = aborted ||
+                          !__all_sync(0xffffffffu, mbar_wait(&o_full[buf], par, abort_flag, fault));
+                float o[PN];
+#pragma unroll
+                for (int i = 0; i < PN; ++i) o[i] = 0.f;
+                if (!aborted) {
+                    tc_fence_after();
+                    tmem_ld_32x32b<PN>(tmem + 32 + buf * PN + lane_off, o);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                }
+                mbar_arrive(&o_empty[buf]);
+#pragma unroll
+                for (int h = 0; h < G; ++h) acc[h] = acc[h] * alpha_prev[h] + (o[h] + o[LO + h]);
+            };
+            // Tile j's scores and P first, then the O of tile j - 1: the PV
+            // round trip of one tile hides behind the softmax of the next.
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const uint32_t buf = j & 1, par = (j >> 1) & 1;
-                aborted = aborted || !mbar_wait(&s_full[buf], par, abort_flag, fault);
+                aborted = aborted ||
+                          !__all_sync(0xffffffffu, mbar_wait(&s_full[buf], par, abort_flag, fault));
                 float s[GN];
 #pragma unroll
                 for (int i = 0; i < GN; ++i) s[i] = 0.f;
@@ -922,20 +968,11 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&p_full[buf]);
-                aborted = aborted || !mbar_wait(&o_full[buf], par, abort_flag, fault);
-                float o[PN];
+                if (k > P.k0) fold(j - 1);
 #pragma unroll
-                for (int i = 0; i < PN; ++i) o[i] = 0.f;
-                if (!aborted) {
-                    tc_fence_after();
-                    tmem_ld_32x32b<PN>(tmem + 32 + buf * PN + lane_off, o);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                }
-                mbar_arrive(&o_empty[buf]);
-#pragma unroll
-                for (int h = 0; h < G; ++h) acc[h] = acc[h] * alpha[h] + (o[h] + o[LO + h]);
+                for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
             }
+            if (P.k1 > P.k0) fold(j - 1);
             // ---- finish the piece: l over the group, then output or partial ----
             float l[G];
 #pragma unroll
@@ -977,7 +1014,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             if (*ticket) {
                 __threadfence();
                 merge_segment<OT>(a, 0, G, P.seg, P.nt, ncta, total_tiles, wt, 128, 1, mwst,
-                                  mslot, nullptr, kInKernelMergeMax, out, group_sync);
+                                  mlst, mslot, nullptr, kInKernelMergeMax, out, group_sync);
                 if (wt == 0) a.counters[(int64_t)P.b * a.kv_heads + P.g] = 0u;
             }
         }
@@ -1002,6 +1039,7 @@ __global__ void __launch_bounds__(128)
 pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     pdl_wait();
     __shared__ float wst[kTcMaxGrid];
+    __shared__ float lst[kTcMaxGrid];
     __shared__ int slot[kTcMaxGrid];
     __shared__ float4 red[128];
     const int b = blockIdx.y;
@@ -1014,8 +1052,8 @@ pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     if (cta_of_tile(seg, ncta, T) == cta_of_tile(seg + nt - 1, ncta, T)) return;
     OT *out = static_cast<OT *>(a.out) +
               ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) * 128;
-    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, 128, 4, wst, slot, red, kTcMaxGrid,
-                      out, [] { __syncthreads(); });
+    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, 128, 4, wst, lst, slot, red,
+                      kTcMaxGrid, out, [] { __syncthreads(); });
 }
 
 int g_sm_count[64];
