@@ -414,12 +414,15 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 // ---------------------------------------------------------------------------
 // tcgen05 path (head_dim 128, page sizes 16/32/64/128, q_heads/kv_heads <= 16)
 //
-// One persistent CTA per SM, 192 threads, warp-specialised:
-//   warp 0     producer: stages the piece's query rows as the B operand and
-//              TMA-loads every page of a 128-token tile straight from the pool
-//              (one 2-D box per page and 64-column half: no gather copy),
-//              3-deep ring of 64 KiB (K 32 KiB + V 32 KiB) stages;
-//   warp 1     one thread issues tcgen05.mma:
+// One persistent CTA per SM, 224 threads, warp-specialised:
+//   warp 0     K producer: stages the piece's query rows as the B operand and
+//              TMA-loads the K rows of every page of a 128-token tile straight
+//              from the pool (one 2-D box per page and 64-column half: no
+//              gather copy); warp 6 does the same for V.  3 stage slots of
+//              K 32 KiB + V 32 KiB; K and V slots have their own barriers, so
+//              a K slot refills as soon as its QK^T ran;
+//   warp 1     one thread issues tcgen05.mma, the S of tile j before the PV
+//              of tile j-1:
 //                S^T[128 tok][16] = K[128 tok][128] . Q^T         (TMEM, f32)
 //                O^T[128 d][PN]  = V^T[128 d][128 tok] . P^T       (TMEM, f32)
 //              M = 128 tokens / dims, N = the query heads of the GQA group
@@ -427,8 +430,9 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 //   warps 2-5  softmax / merge group: thread i owns token i of S^T (and dim i
 //              of O^T); per tile it takes the block-wide running max per head,
 //              writes P = exp2(s - m) to shared memory, zeroes V rows past the
-//              length, and folds the tile's O into FP32 registers with the
-//              running-max correction.
+//              length, and folds the previous tile's O into FP32 registers with
+//              the running-max correction (one tile late, so the PV round trip
+//              overlaps the next tile's softmax).
 // P is written as two storage-dtype halves, hi = round(p) in B rows [0, G)
 // and lo = round(p - hi) in rows [PN/2, PN/2 + G), so the one PV MMA returns
 // O_hi and O_lo side by side and their sum carries ~22 bits of P (a single
@@ -445,7 +449,7 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 // sequence); then pkv_tc_merge_kernel, one CTA per (sequence, query head),
 // merges after the decode kernel.
 // ---------------------------------------------------------------------------
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 224;
 constexpr int kTcTile = 128;
 constexpr int kTcStages = 3;
 constexpr int kTcMaxBatch = 1024;
@@ -686,9 +690,10 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     unsigned char *sm = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kTcBarOff);
-    uint64_t *full = bars, *empty = bars + 3, *s_full = bars + 6, *s_empty = bars + 8;
+    uint64_t *kfull = bars, *kempty = bars + 3, *s_full = bars + 6, *s_empty = bars + 8;
     uint64_t *p_full = bars + 10, *o_full = bars + 12, *o_empty = bars + 14;
     uint64_t *q_full = bars + 16, *q_empty = bars + 18;
+    uint64_t *vfull = bars + 20, *vempty = bars + 23;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kTcMiscOff);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kTcMiscOff + 4);
     int *ticket = reinterpret_cast<int *>(sm + kTcMiscOff + 8);
@@ -703,8 +708,10 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&kfull[s], 1);
+            mbar_init(&kempty[s], 1);
+            mbar_init(&vfull[s], 1);
+            mbar_init(&vempty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
@@ -752,8 +759,38 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     if (blockIdx.x == 0 && a.tile_prefix != nullptr)
         for (int b = tid; b <= a.batch; b += kTcThreads) a.tile_prefix[b] = prefix[b];
 
+    // One tile's pages of one pool (K: warp 0, V: warp 6) into stage slot
+    // `dst` (two 64-column halves), completing on `bar`.  Lanes < np each load
+    // one page.
+    auto load_tile = [&](const CUtensorMap *map, uint64_t *bar, unsigned char *dst,
+                         const uint32_t *trow, int k, int L, int g) {
+        const int ts = k * kTcTile;
+        const int te = min(L, ts + kTcTile);
+        const int p0 = ts / a.block_size;
+        const int np = (te - ts + a.block_size - 1) / a.block_size;
+        uint32_t pid = 0;
+        bool good = false;
+        if (lane < np) {
+            const int pi = p0 + lane;
+            if (pi < a.table_stride) {
+                pid = __ldg(trow + pi);
+                good = pid < a.block_count;
+            }
+            if (!good) record_fault(fault, kFaultPageOutOfRange);
+        }
+        const unsigned mask = __ballot_sync(0xffffffffu, good);
+        if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)__popc(mask) * a.block_size * 256u);
+        __syncwarp();
+        if (good) {
+            const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
+            const int32_t y = (int32_t)pid * a.block_size;
+            tma_load_2d(dst + ro, map, bar, g * 128, y);
+            tma_load_2d(dst + kTcHalf + ro, map, bar, g * 128 + 64, y);
+        }
+    };
     if (warp == 0) {
-        // ------------------------------ producer ------------------------------
+        // ---------------------------- K producer ----------------------------
+        // Also stages each piece's query rows (the B operand of QK^T).
         uint32_t j = 0, qi = 0;
         bool ok = true;
         for (int64_t t = my_start; ok && t < my_end;) {
@@ -775,40 +812,34 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const int stage = (int)(j % kTcStages);
-                if (!mbar_wait(&empty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
+                if (!mbar_wait(&kempty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
                     ok = false;
                     break;
                 }
-                const int ts = k * kTcTile;
-                const int te = min(L, ts + kTcTile);
-                const int p0 = ts / a.block_size;
-                const int np = (te - ts + a.block_size - 1) / a.block_size;
-                uint32_t pid = 0;
-                bool good = false;
-                if (lane < np) {
-                    const int pi = p0 + lane;
-                    if (pi < a.table_stride) {
-                        pid = __ldg(trow + pi);
-                        good = pid < a.block_count;
-                    }
-                    if (!good) record_fault(fault, kFaultPageOutOfRange);
-                }
-                const unsigned mask = __ballot_sync(0xffffffffu, good);
-                if (lane == 0)
-                    mbar_arrive_expect_tx(&full[stage], (uint32_t)__popc(mask) * a.block_size * 512u);
-                __syncwarp();
-                if (good) {
-                    unsigned char *st = sm + stage * kTcStageBytes;
-                    const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
-                    const int32_t y = (int32_t)pid * a.block_size;
-                    const int32_t x = P.g * 128;
-                    tma_load_2d(st + ro, &kmap, &full[stage], x, y);
-                    tma_load_2d(st + kTcHalf + ro, &kmap, &full[stage], x + 64, y);
-                    tma_load_2d(st + 2 * kTcHalf + ro, &vmap, &full[stage], x, y);
-                    tma_load_2d(st + 3 * kTcHalf + ro, &vmap, &full[stage], x + 64, y);
-                }
+                load_tile(&kmap, &kfull[stage], sm + stage * kTcStageBytes, trow, k, L, P.g);
             }
             ++qi;
+        }
+    } else if (warp == 6) {
+        // ---------------------------- V producer ----------------------------
+        // V slots free later than K slots (after the PV, not the QK^T), so the
+        // two rings run on their own barriers and K loads can run ahead.
+        uint32_t j = 0;
+        bool ok = true;
+        for (int64_t t = my_start; ok && t < my_end;) {
+            const Piece P = piece_at(t, my_end, prefix, a);
+            t += P.k1 - P.k0;
+            const int L = __ldg(a.seq_lens + P.b);
+            const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
+            for (int k = P.k0; k < P.k1; ++k, ++j) {
+                const int stage = (int)(j % kTcStages);
+                if (!mbar_wait(&vempty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
+                    ok = false;
+                    break;
+                }
+                load_tile(&vmap, &vfull[stage], sm + stage * kTcStageBytes + 2 * kTcHalf, trow, k,
+                          L, P.g);
+            }
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
@@ -825,7 +856,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 auto issue_pv = [&](uint32_t jp) -> bool {
                     const int stage = (int)(jp % kTcStages);
                     const uint32_t buf = jp & 1, par = (jp >> 1) & 1;
-                    if (!mbar_wait(&p_full[buf], par, abort_flag, fault) ||
+                    if (!mbar_wait(&vfull[stage], (jp / kTcStages) & 1, abort_flag, fault) ||
+                        !mbar_wait(&p_full[buf], par, abort_flag, fault) ||
                         !mbar_wait(&o_empty[buf], par ^ 1, abort_flag, fault))
                         return false;
                     tc_fence_after();
@@ -838,7 +870,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                         mma_f16_ss(tmem + 32 + buf * PN, ad, bd, kIdescPV, kk > 0);
                     }
                     mma_commit(&o_full[buf]);
-                    mma_commit(&empty[stage]);
+                    mma_commit(&vempty[stage]);
                     return true;
                 };
                 // S of tile j is issued before the PV of tile j - 1, so the
@@ -846,7 +878,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 for (int k = P.k0; k < P.k1; ++k, ++j) {
                     const int stage = (int)(j % kTcStages);
                     const uint32_t buf = j & 1, par = (j >> 1) & 1;
-                    if (!mbar_wait(&full[stage], (j / kTcStages) & 1, abort_flag, fault) ||
+                    if (!mbar_wait(&kfull[stage], (j / kTcStages) & 1, abort_flag, fault) ||
                         !mbar_wait(&s_empty[buf], par ^ 1, abort_flag, fault)) {
                         ok = false;
                         break;
@@ -860,6 +892,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                         mma_f16_ss(tmem + buf * 16, ad, bd, kIdescQK, kk > 0);
                     }
                     mma_commit(&s_full[buf]);
+                    mma_commit(&kempty[stage]);
                     if (k == P.k1 - 1) mma_commit(&q_empty[qi & 1]);
                     if (k > P.k0 && !issue_pv(j - 1)) {
                         ok = false;
@@ -871,7 +904,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < 6) {
         // --------------------------- softmax / merge ---------------------------
         // On an abort (a wait gave up) the group keeps running the same loops
         // and named barriers -- so no thread can be left waiting at one -- but
@@ -957,7 +990,10 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                     *reinterpret_cast<T *>(pbuf + sw128_offset(h, row, kPChunk)) = hi;
                     *reinterpret_cast<T *>(pbuf + sw128_offset(LO + h, row, kPChunk)) = lo;
                 }
-                if (!live) {  // V rows past the length may hold anything: zero them
+                // V rows past the length may hold anything: zero them once the
+                // tile's V landed (its own barrier: V may arrive after S ran)
+                if (!live && !aborted &&
+                    mbar_wait(&vfull[j % kTcStages], (j / kTcStages) & 1, abort_flag, fault)) {
                     unsigned char *vrow =
                         sm + (j % kTcStages) * kTcStageBytes + 2 * kTcHalf + row * 128;
 #pragma unroll
