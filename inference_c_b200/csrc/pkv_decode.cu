@@ -1411,7 +1411,14 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         t.block_size = (int32_t)layer->block_size;
         t.block_count = (uint32_t)layer->block_count;
         t.scale_log2 = scale * pkv::kLog2e;
-        t.merge_in_kernel = ncta / (int)kvh + 2 <= pkv::kInKernelMergeMax;
+        // In-kernel merges need every segment to span at most
+        // kInKernelMergeMax CTAs.  They also sit on the critical path of the
+        // CTA that finishes last, so with few segments (each cut into many
+        // pieces, e.g. one long sequence) the separate merge kernel, one CTA
+        // per query head, finishes sooner.
+        const bool fits = ncta / (int)kvh + 2 <= pkv::kInKernelMergeMax;
+        const bool many_segments = batch->batch * kvh * 2 >= (size_t)ncta;
+        t.merge_in_kernel = fits && many_segments;
         // launches of at most kTcMaxBatch sequences (their prefix lives in smem)
         const size_t osz = output_dtype == PKV_DTYPE_F32 ? 4 : 2;
         ok = 1;
