@@ -415,8 +415,8 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 // tcgen05 path (head_dim 128, page sizes 16/32/64/128, q_heads/kv_heads <= 16)
 //
 // One persistent CTA per SM, 224 threads, warp-specialised:
-//   warp 0     K producer: stages the piece's query rows as the B operand and
-//              TMA-loads the K rows of every page of a 128-token tile straight
+//   warp 0     K producer: TMA-loads the piece's query rows (the B operand)
+//              and the K rows of every page of a 128-token tile straight
 //              from the pool (one 2-D box per page and 64-column half: no
 //              gather copy); warp 6 does the same for V.  3 stage slots of
 //              K 32 KiB + V 32 KiB; K and V slots have their own barriers, so
@@ -486,6 +486,13 @@ struct TcArgs {
     uint32_t block_count;
     float scale_log2;
     int32_t merge_in_kernel;
+    int32_t q_row0;         // query row (sequence * q_heads) of this launch's first sequence
+};
+
+// Tensor maps of one launch: K and V pools (one page x 64 columns per box)
+// and the query rows (G heads x 64 columns per box).
+struct TcMaps {
+    CUtensorMap k, v, q;
 };
 
 struct TcWorkspace {
@@ -678,7 +685,8 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
 template <int G, typename T, typename OT>
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
-                       const __grid_constant__ CUtensorMap vmap) {
+                       const __grid_constant__ CUtensorMap vmap,
+                       const __grid_constant__ CUtensorMap qmap) {
     using namespace sm100;
     constexpr int GN = G <= 4 ? 4 : G;  // S^T columns read per thread
     constexpr int PN = G <= 8 ? 16 : 32;  // P^T rows (= O^T columns): hi and lo halves
@@ -735,6 +743,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         tma_prefetch_desc(&kmap);
         tma_prefetch_desc(&vmap);
+        tma_prefetch_desc(&qmap);
     }
     // Everything above touches only this CTA's shared memory and TMEM, so it
     // overlaps the previous kernel under programmatic dependent launch; from
@@ -798,17 +807,14 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
             if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) break;
-            unsigned char *qb = sm + kTcQOff + (qi & 1) * 4096;
-            const T *qsrc = static_cast<const T *>(a.query) +
-                            ((int64_t)P.b * q_heads + (int64_t)P.g * G) * 128;
-            for (int idx = lane; idx < G * 16; idx += 32) {
-                const int h = idx >> 4, c16 = idx & 15;
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qsrc + h * 128 + c16 * 8));
-                *reinterpret_cast<uint4 *>(qb + sw128_offset(h, c16 * 8, 2048)) = v;
+            if (lane == 0) {  // G query rows, two 64-column halves, 128-byte swizzle
+                unsigned char *qb = sm + kTcQOff + (qi & 1) * 4096;
+                const int32_t qrow = a.q_row0 + P.b * q_heads + P.g * G;
+                mbar_arrive_expect_tx(&q_full[qi & 1], (uint32_t)G * 256u);
+                tma_load_2d(qb, &qmap, &q_full[qi & 1], 0, qrow);
+                tma_load_2d(qb + 2048, &qmap, &q_full[qi & 1], 64, qrow);
             }
-            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&q_full[qi & 1]);
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const int stage = (int)(j % kTcStages);
@@ -1167,15 +1173,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D view of one pool: [rows][kv_width] two-byte elements, box = one page
-// of one 64-column half, 128-byte swizzle (the UMMA canonical layout).
+// 2-D view of [rows][width] two-byte elements (a pool, or the query rows),
+// box = box_rows rows (one page, or one GQA group) of one 64-column half,
+// 128-byte swizzle (the UMMA canonical layout).
 bool encode_pool_map(CUtensorMap *map, const void *pool, uint64_t rows, uint64_t kv_width,
-                     uint32_t block_size, bool bf16) {
+                     uint32_t box_rows, bool bf16) {
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return false;
     cuuint64_t dims[2] = {kv_width, rows};
     cuuint64_t strides[1] = {kv_width * 2};
-    cuuint32_t box[2] = {64, block_size};
+    cuuint32_t box[2] = {64, box_rows};
     cuuint32_t estr[2] = {1, 1};
     return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                const_cast<void *>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1184,7 +1191,7 @@ bool encode_pool_map(CUtensorMap *map, const void *pool, uint64_t rows, uint64_t
 }
 
 template <int G, typename T, typename OT>
-int launch_tc(const TcArgs &args, const CUtensorMap &km, const CUtensorMap &vm, int ncta,
+int launch_tc(const TcArgs &args, const TcMaps &mp, int ncta,
               cudaStream_t stream) {
     auto kern = paged_decode_tc_kernel<G, T, OT>;
     static int configured[64];
@@ -1210,7 +1217,7 @@ int launch_tc(const TcArgs &args, const CUtensorMap &km, const CUtensorMap &vm, 
     cfg.stream = stream;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, args, km, vm) != cudaSuccess) return 0;
+    if (cudaLaunchKernelEx(&cfg, kern, args, mp.k, mp.v, mp.q) != cudaSuccess) return 0;
     if (!args.merge_in_kernel) {
         cudaLaunchConfig_t mc = cfg;
         mc.gridDim = dim3(args.kv_heads * G, args.batch);
@@ -1223,27 +1230,26 @@ int launch_tc(const TcArgs &args, const CUtensorMap &km, const CUtensorMap &vm, 
 }
 
 template <typename T, typename OT>
-int dispatch_tc_group(const TcArgs &args, int group, const CUtensorMap &km, const CUtensorMap &vm,
-                      int ncta, cudaStream_t s) {
+int dispatch_tc_group(const TcArgs &args, int group, const TcMaps &mp, int ncta, cudaStream_t s) {
     switch (group) {
-        case 1: return launch_tc<1, T, OT>(args, km, vm, ncta, s);
-        case 2: return launch_tc<2, T, OT>(args, km, vm, ncta, s);
-        case 4: return launch_tc<4, T, OT>(args, km, vm, ncta, s);
-        case 8: return launch_tc<8, T, OT>(args, km, vm, ncta, s);
-        case 16: return launch_tc<16, T, OT>(args, km, vm, ncta, s);
+        case 1: return launch_tc<1, T, OT>(args, mp, ncta, s);
+        case 2: return launch_tc<2, T, OT>(args, mp, ncta, s);
+        case 4: return launch_tc<4, T, OT>(args, mp, ncta, s);
+        case 8: return launch_tc<8, T, OT>(args, mp, ncta, s);
+        case 16: return launch_tc<16, T, OT>(args, mp, ncta, s);
         default: return 0;
     }
 }
 
-int dispatch_tc(const TcArgs &args, int group, bool bf16, PkvDType out, const CUtensorMap &km,
-                const CUtensorMap &vm, int ncta, cudaStream_t s) {
+int dispatch_tc(const TcArgs &args, int group, bool bf16, PkvDType out, const TcMaps &mp,
+                int ncta, cudaStream_t s) {
     if (!bf16)
         return out == PKV_DTYPE_F32
-                   ? dispatch_tc_group<__half, float>(args, group, km, vm, ncta, s)
-                   : dispatch_tc_group<__half, __half>(args, group, km, vm, ncta, s);
+                   ? dispatch_tc_group<__half, float>(args, group, mp, ncta, s)
+                   : dispatch_tc_group<__half, __half>(args, group, mp, ncta, s);
     return out == PKV_DTYPE_F32
-               ? dispatch_tc_group<__nv_bfloat16, float>(args, group, km, vm, ncta, s)
-               : dispatch_tc_group<__nv_bfloat16, __nv_bfloat16>(args, group, km, vm, ncta, s);
+               ? dispatch_tc_group<__nv_bfloat16, float>(args, group, mp, ncta, s)
+               : dispatch_tc_group<__nv_bfloat16, __nv_bfloat16>(args, group, mp, ncta, s);
 }
 
 bool tc_eligible(size_t head_dim, size_t block_size, size_t group, size_t rows) {
@@ -1389,13 +1395,15 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
     const cudaStream_t s = (cudaStream_t)stream;
     int ok;
     if (use_tc) {
-        CUtensorMap km, vm;
+        pkv::TcMaps mp;
         const bool bf16 = layer->dtype == PKV_DTYPE_BF16;
         const uint64_t rows = (uint64_t)layer->block_count * layer->block_size;
-        if (!pkv::encode_pool_map(&km, layer->key_pool, rows, kvh * hd, (uint32_t)layer->block_size,
-                                  bf16) ||
-            !pkv::encode_pool_map(&vm, layer->value_pool, rows, kvh * hd,
-                                  (uint32_t)layer->block_size, bf16)) {
+        if (!pkv::encode_pool_map(&mp.k, layer->key_pool, rows, kvh * hd,
+                                  (uint32_t)layer->block_size, bf16) ||
+            !pkv::encode_pool_map(&mp.v, layer->value_pool, rows, kvh * hd,
+                                  (uint32_t)layer->block_size, bf16) ||
+            !pkv::encode_pool_map(&mp.q, query, (uint64_t)batch->batch * q_heads, hd,
+                                  (uint32_t)group, bf16)) {
             pkv_internal_set_error(error, error_capacity, "%s: tensor map encoding failed", what);
             return 0;
         }
@@ -1431,9 +1439,10 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
             sl.tables = batch->block_tables + b0 * batch->table_stride;
             sl.seq_lens = batch->seq_lens + b0;
             sl.query = static_cast<const char *>(query) + b0 * q_heads * hd * 2;
+            sl.q_row0 = (int32_t)(b0 * q_heads);
             sl.out = static_cast<char *>(output) + b0 * q_heads * hd * osz;
             sl.counters = t.counters + b0 * kvh;
-            ok = pkv::dispatch_tc(sl, (int)group, bf16, output_dtype, km, vm, ncta, s);
+            ok = pkv::dispatch_tc(sl, (int)group, bf16, output_dtype, mp, ncta, s);
         }
     } else if (layer->dtype == PKV_DTYPE_F16)
         ok = hd == 128 ? pkv::dispatch_group<128, __half>(a, (int)group, output_dtype, s)
