@@ -3,7 +3,8 @@
 The product is the shared library ``inference_c_b200/lib/libpkv_b200.so``:
 C11 host code (page allocator with the SDK's ``tensor_paged_kv_*`` API, the
 device pool and the batch step transaction) and the CUDA kernels, exported
-through ``include/paged_kv_cache.h`` and ``include/pkv_b200.h``.  This module
+through ``include/paged_kv_cache.h``, ``include/pkv_b200.h`` and
+``include/attention.h`` (the SDK's paged decoder entry point).  This module
 is the Python view of that ABI, via ctypes: tests and ``bench.py`` use it,
 with torch only for device memory and streams.  Nothing here computes
 attention; there is no CPU fallback, and every call raises when the library
@@ -51,6 +52,56 @@ class PkvBatch(ctypes.Structure):
     ]
 
 
+# include/attention.h: TENSOR_PAGED_KV_* storage kinds and the request struct
+TENSOR_PAGED_KV_F32 = 0
+TENSOR_PAGED_KV_F16 = 1
+TENSOR_PAGED_KV_QUANT_F16 = 2
+TENSOR_WEIGHT_Q8_0 = 1
+TENSOR_WEIGHT_Q4_0 = 2
+
+
+class TensorAttentionDecoderLayer(ctypes.Structure):
+    """TensorAttentionDecoderLayer / ...LayerF16: nine pointers in this order."""
+    _fields_ = [(n, _c_ptr) for n in ("input_norm", "q_weight", "k_weight", "v_weight",
+                                      "o_weight", "post_norm", "gate_weight", "up_weight",
+                                      "down_weight")]
+
+
+class TensorAttentionDecoderLayerQuantF16(ctypes.Structure):
+    """The quantised layer struct keeps both norms first."""
+    _fields_ = [(n, _c_ptr) for n in ("input_norm", "post_norm", "q_weight", "k_weight",
+                                      "v_weight", "o_weight", "gate_weight", "up_weight",
+                                      "down_weight")]
+
+
+class TensorPagedKVDecodeRequest(ctypes.Structure):
+    _fields_ = [
+        ("cache", _c_ptr),
+        ("sequence", _c_u64),
+        ("storage", _c_int),
+        ("layers", _c_ptr),
+        ("layer_count", _c_size),
+        ("embedding", _c_ptr),
+        ("initial_token", ctypes.c_uint32),
+        ("token_count", _c_size),
+        ("generated_tokens", _c_ptr),
+        ("key_cache", _c_ptr),
+        ("value_cache", _c_ptr),
+        ("past_length", _c_size),
+        ("hidden_size", _c_size),
+        ("intermediate_size", _c_size),
+        ("query_heads", _c_size),
+        ("kv_heads", _c_size),
+        ("head_dim", _c_size),
+        ("rms_norm_epsilon", ctypes.c_float),
+        ("rope_theta", ctypes.c_double),
+        ("final_norm", _c_ptr),
+        ("lm_head", _c_ptr),
+        ("vocabulary_size", _c_size),
+        ("weight_quantization", _c_int),
+    ]
+
+
 _LP = ctypes.POINTER(PkvPagedLayer)
 _BP = ctypes.POINTER(PkvBatch)
 _ERR = [_c_char_p, _c_size]
@@ -74,6 +125,10 @@ EXPORTS = {
     "tensor_paged_kv_cache_block_count": (_c_size, [_c_ptr]),
     "tensor_paged_kv_cache_backend_state": (_c_ptr, [_c_ptr, _c_int]),
     "tensor_paged_kv_cache_set_backend_state": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr]),
+    # include/attention.h
+    "tensor_attention_decode_sequence_paged": (
+        _c_int, [ctypes.POINTER(TensorPagedKVDecodeRequest)]),
+    "tensor_attention_decode_cache_clear": (None, []),
     # include/pkv_b200.h -- kernels
     "pkv_kv_append": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
     "pkv_kv_import": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, *_ERR]),
@@ -355,3 +410,76 @@ class PagedPool:
 
     def step_end(self, commit: bool) -> None:
         _call("pkv_step_end", self.handle, int(commit))
+
+
+# ---------------------------------------------------------------------------
+# include/attention.h: the SDK's paged decoder (greedy tokens of one sequence)
+# ---------------------------------------------------------------------------
+
+def decode_sequence_paged(cache: "PagedKVCache", sequence: int, storage: int, layers,
+                          embedding, initial_token: int, token_count: int, key_cache,
+                          value_cache, past_length: int, hidden_size: int,
+                          intermediate_size: int, query_heads: int, kv_heads: int,
+                          head_dim: int, rms_norm_epsilon: float, rope_theta: float,
+                          final_norm, lm_head, vocabulary_size: int,
+                          weight_quantization: int = 0) -> Optional[list]:
+    """tensor_attention_decode_sequence_paged with host numpy arrays.
+
+    layers: one sequence of nine arrays per layer (input_norm, q, k, v, o,
+    post_norm, gate, up, down, whatever the storage's struct order) in the
+    storage's element type (float32 or
+    uint16 half bits; uint8 blocks for quantised matrices); key_cache /
+    value_cache: one host array per layer holding at least past_length rows.
+    Returns the generated tokens, or None when the call returns 0 (the SDK
+    reports failure only through the return value)."""
+    import numpy as np
+    lib = load()
+    keep = []
+
+    def ptr(a):
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    kind = (TensorAttentionDecoderLayerQuantF16 if storage == TENSOR_PAGED_KV_QUANT_F16
+            else TensorAttentionDecoderLayer)
+    order = ("input_norm", "q_weight", "k_weight", "v_weight", "o_weight", "post_norm",
+             "gate_weight", "up_weight", "down_weight")
+    layer_arr = (kind * len(layers))()
+    for i, tensors in enumerate(layers):
+        assert len(tensors) == 9
+        for name, t in zip(order, tensors):
+            setattr(layer_arr[i], name, ptr(t))
+    kc = (_c_ptr * len(key_cache))(*[ptr(a) for a in key_cache])
+    vc = (_c_ptr * len(value_cache))(*[ptr(a) for a in value_cache])
+    out = np.zeros(max(token_count, 1), dtype=np.uint32)
+    rq = TensorPagedKVDecodeRequest()
+    rq.cache = cache.handle if cache is not None else None
+    rq.sequence = sequence
+    rq.storage = storage
+    rq.layers = ctypes.addressof(layer_arr)
+    rq.layer_count = len(layers)
+    rq.embedding = ptr(embedding)
+    rq.initial_token = initial_token
+    rq.token_count = token_count
+    rq.generated_tokens = out.ctypes.data
+    rq.key_cache = ctypes.addressof(kc)
+    rq.value_cache = ctypes.addressof(vc)
+    rq.past_length = past_length
+    rq.hidden_size = hidden_size
+    rq.intermediate_size = intermediate_size
+    rq.query_heads = query_heads
+    rq.kv_heads = kv_heads
+    rq.head_dim = head_dim
+    rq.rms_norm_epsilon = rms_norm_epsilon
+    rq.rope_theta = rope_theta
+    rq.final_norm = ptr(final_norm)
+    rq.lm_head = ptr(lm_head)
+    rq.vocabulary_size = vocabulary_size
+    rq.weight_quantization = weight_quantization
+    ok = lib.tensor_attention_decode_sequence_paged(ctypes.byref(rq))
+    return out[:token_count].tolist() if ok else None
+
+
+def decode_cache_clear() -> None:
+    load().tensor_attention_decode_cache_clear()

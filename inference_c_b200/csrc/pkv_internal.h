@@ -42,6 +42,7 @@ int pkv_internal_copy_table_tail(TensorPagedKVCache *cache,
 int pkv_internal_take_copy_fault(uint32_t *code);
 int pkv_internal_take_decode_fault(uint32_t *code);
 int pkv_internal_take_prefill_fault(uint32_t *code);
+int pkv_internal_take_sequence_fault(uint32_t *code);
 
 /* Writes a message into a caller error buffer (NULL-safe). */
 void pkv_internal_set_error(char *error, size_t capacity, const char *fmt, ...);

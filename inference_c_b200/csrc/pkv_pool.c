@@ -107,8 +107,8 @@ int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
         return 0;
     }
     *pool = NULL;
-    if ((dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16) || layer_count == 0 ||
-        kv_heads == 0 || head_dim == 0 || (kv_heads * head_dim * 2) % 16 != 0 ||
+    if ((dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16 && dtype != PKV_DTYPE_F32) ||
+        layer_count == 0 || kv_heads == 0 || head_dim == 0 ||
         max_batch == 0 || max_batch > INT32_MAX || max_pages_per_seq == 0 ||
         max_pages_per_seq > INT32_MAX) {
         pkv_internal_set_error(error, cap, "pkv_pool_create: invalid shape or dtype");
@@ -147,7 +147,8 @@ int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
     const int have_prev = cudaGetDevice(&prev) == cudaSuccess;
     cudaError_t st = cudaSetDevice(device);
     const size_t kv_width = kv_heads * head_dim;
-    const size_t pool_bytes = p->block_count * p->block_size * kv_width * 2u;
+    const size_t elem = dtype == PKV_DTYPE_F32 ? 4u : 2u;
+    const size_t pool_bytes = p->block_count * p->block_size * kv_width * elem;
     for (size_t l = 0; st == cudaSuccess && l < layer_count; ++l) {
         st = cudaMalloc(&p->kpools[l], pool_bytes);
         if (st == cudaSuccess) st = cudaMalloc(&p->vpools[l], pool_bytes);
@@ -374,15 +375,16 @@ int pkv_device_fault(int device, uint32_t *code, char *error, size_t cap) {
     const int have_prev = cudaGetDevice(&prev) == cudaSuccess;
     cudaError_t st = cudaSetDevice(device);
     if (st == cudaSuccess) st = cudaDeviceSynchronize();
-    uint32_t a = 0, b = 0, c = 0;
+    uint32_t a = 0, b = 0, c = 0, d = 0;
     int ok = st == cudaSuccess && pkv_internal_take_copy_fault(&a) &&
-             pkv_internal_take_decode_fault(&b) && pkv_internal_take_prefill_fault(&c);
+             pkv_internal_take_decode_fault(&b) && pkv_internal_take_prefill_fault(&c) &&
+             pkv_internal_take_sequence_fault(&d);
     if (have_prev) cudaSetDevice(prev);
     if (!ok) {
         pkv_internal_set_error(error, cap, "pkv_device_fault: %s",
                                cudaGetErrorString(st != cudaSuccess ? st : cudaGetLastError()));
         return 0;
     }
-    *code = a ? a : (b ? b : c);
+    *code = a ? a : (b ? b : (c ? c : d));
     return 1;
 }

@@ -5,6 +5,8 @@
   (tensor_sdpa_f32, the allocator, the f16 conversions) plus ref_harness.c.
   It is built from the SDK's source tree by oracle/Makefile and is absent
   where that tree was never available; ``ref_available()`` says which.
+* ``ref_cuda``: _ref/libref_cuda.so, the SDK's own CUDA backend (its paged
+  decoder loop) built the same way; it needs a GPU to run.
 
 Only tests/, __graft_entry__.smoke() and bench.py's reference / cpu_baseline
 legs use this module, as the checker; the product never does.
@@ -21,6 +23,7 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 PORT_PATH = HERE / "libpkv_oracle.so"
 REF_PATH = HERE / "_ref" / "libref_oracle.so"
+REF_CUDA_PATH = HERE / "_ref" / "libref_cuda.so"
 
 F16, BF16 = 1, 2
 _DT = {"f16": F16, "bf16": BF16}
@@ -57,6 +60,10 @@ def port() -> ctypes.CDLL:
         lib.orc_kv_rows.argtypes = [_p, _p, _s, _s, _s, _p, _s, _p, _p, _s, _p, _p, _i, _i]
         lib.orc_sdpa_f32.restype = _i
         lib.orc_sdpa_f32.argtypes = [_p, _p, _p, _p, _p, _s, _s, _s, _s, _s, _s, _s, _f, _i, _p]
+        lib.orc_decode_sequence.restype = _i
+        lib.orc_decode_sequence.argtypes = [_i, _i, _p, _s, _p, ctypes.c_uint32, _s, _p, _p, _p,
+                                            _s, _s, _s, _s, _s, _s, _s, _f, ctypes.c_double, _p,
+                                            _p, _s, _p]
         lib.orc_paged_attention_rows.restype = _i
         lib.orc_paged_attention_rows.argtypes = [_p, _p, _s, _i, _i, _p, _p, _s, _s, _s, _s, _p,
                                                  _s, ctypes.c_int64, _s, _f, _p]
@@ -264,3 +271,110 @@ class RefJob:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------------------
+# The paged decoder (include/attention.h): restatement and the SDK's own GPU
+# ---------------------------------------------------------------------------
+
+def decode_sequence(storage: int, fmt: int, layers, embedding, initial_token: int,
+                    token_count: int, kcache, vcache, past: int, capacity: int, hidden: int,
+                    inter: int, qh: int, kvh: int, hd: int, eps: float, theta: float,
+                    final_norm, lm_head, vocab: int, want_logits: bool = False):
+    """orc_decode_sequence.  layers: per layer nine arrays (input_norm, q, k,
+    v, o, post_norm, gate, up, down); kcache/vcache: per layer contiguous
+    [capacity, kv_width] arrays in the storage type, positions [0, past)
+    holding the prefix, updated in place.  Returns the tokens (and every
+    step's logits, [token_count, vocab])."""
+    keep = []
+
+    def a(x):
+        x = np.ascontiguousarray(x)
+        keep.append(x)
+        return x.ctypes.data
+
+    ptrs = (_p * (9 * len(layers)))(*[a(t) for layer in layers for t in layer])
+    for c in list(kcache) + list(vcache):
+        assert c.flags["C_CONTIGUOUS"]
+    kc = (_p * len(kcache))(*[c.ctypes.data for c in kcache])
+    vc = (_p * len(vcache))(*[c.ctypes.data for c in vcache])
+    out = np.zeros(token_count, dtype=np.uint32)
+    logits = np.zeros((token_count, vocab), dtype=np.float32)
+    ok = port().orc_decode_sequence(storage, fmt, ptrs, len(layers), a(embedding), initial_token,
+                                    token_count, out.ctypes.data, kc, vc, past, capacity, hidden,
+                                    inter, qh, kvh, hd, eps, theta, a(final_norm), a(lm_head),
+                                    vocab, logits.ctypes.data)
+    if not ok:
+        raise ValueError("oracle decode_sequence: invalid arguments")
+    tokens = out.tolist()
+    return (tokens, logits) if want_logits else tokens
+
+
+def ref_cuda_available() -> bool:
+    return REF_CUDA_PATH.exists()
+
+
+class _Request(ctypes.Structure):
+    """TensorPagedKVDecodeRequest (the SDK's include/attention.h:48-72)."""
+    _fields_ = [("cache", _p), ("sequence", ctypes.c_uint64), ("storage", _i), ("layers", _p),
+                ("layer_count", _s), ("embedding", _p), ("initial_token", ctypes.c_uint32),
+                ("token_count", _s), ("generated_tokens", _p), ("key_cache", _p),
+                ("value_cache", _p), ("past_length", _s), ("hidden_size", _s),
+                ("intermediate_size", _s), ("query_heads", _s), ("kv_heads", _s),
+                ("head_dim", _s), ("rms_norm_epsilon", _f), ("rope_theta", ctypes.c_double),
+                ("final_norm", _p), ("lm_head", _p), ("vocabulary_size", _s),
+                ("weight_quantization", _i)]
+
+
+class RefCudaDecoder:
+    """One paged cache and sequence inside the SDK's own CUDA build; each
+    call runs its tensor_attention_decode_sequence_paged."""
+
+    def __init__(self, block_size: int, block_count: int):
+        if not REF_CUDA_PATH.exists():
+            raise FileNotFoundError(f"{REF_CUDA_PATH} not built (needs the SDK sources)")
+        lib = ctypes.CDLL(str(REF_CUDA_PATH))
+        lib.tensor_paged_kv_cache_create.restype = _i
+        lib.tensor_paged_kv_cache_create.argtypes = [_s, _s, _s, ctypes.POINTER(_p)]
+        lib.tensor_paged_kv_sequence_create.restype = _i
+        lib.tensor_paged_kv_sequence_create.argtypes = [_p, ctypes.POINTER(ctypes.c_uint64)]
+        lib.tensor_attention_decode_sequence_paged.restype = _i
+        lib.tensor_attention_decode_sequence_paged.argtypes = [ctypes.POINTER(_Request)]
+        lib.tensor_paged_kv_cache_free.argtypes = [_p]
+        lib.tensor_attention_decode_cache_clear.argtypes = []
+        self.lib = lib
+        h = _p()
+        assert lib.tensor_paged_kv_cache_create(block_size, block_count, 1, ctypes.byref(h))
+        self.cache = h.value
+        seq = ctypes.c_uint64()
+        assert lib.tensor_paged_kv_sequence_create(self.cache, ctypes.byref(seq))
+        self.seq = seq.value
+
+    def decode(self, storage, fmt, layers, embedding, initial_token, token_count, kcache,
+               vcache, past, hidden, inter, qh, kvh, hd, eps, theta, final_norm, lm_head,
+               vocab):
+        keep = []
+
+        def a(x):
+            x = np.ascontiguousarray(x)
+            keep.append(x)
+            return x.ctypes.data
+
+        # the quantised layer struct keeps both norms first (attention.h:38-42)
+        order = [0, 5, 1, 2, 3, 4, 6, 7, 8] if storage == 2 else list(range(9))
+        ptrs = (_p * (9 * len(layers)))(*[a(layer[i]) for layer in layers for i in order])
+        kc = (_p * len(kcache))(*[a(c) for c in kcache])
+        vc = (_p * len(vcache))(*[a(c) for c in vcache])
+        out = np.zeros(token_count, dtype=np.uint32)
+        rq = _Request(self.cache, self.seq, storage, ctypes.addressof(ptrs), len(layers),
+                      a(embedding), initial_token, token_count, out.ctypes.data,
+                      ctypes.addressof(kc), ctypes.addressof(vc), past, hidden, inter, qh, kvh,
+                      hd, eps, theta, a(final_norm), a(lm_head), vocab, fmt)
+        ok = self.lib.tensor_attention_decode_sequence_paged(ctypes.byref(rq))
+        return out.tolist() if ok else None
+
+    def close(self):
+        if self.cache:
+            self.lib.tensor_paged_kv_cache_free(self.cache)
+            self.lib.tensor_attention_decode_cache_clear()
+            self.cache = None

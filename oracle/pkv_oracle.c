@@ -26,6 +26,10 @@
  *       rules (:355-377), expf and division (:369-379) and the key-ordered
  *       P.V sum (:389-401).  Same loop order, so with the same compiler flags
  *       its results match the SDK's bit for bit.
+ *   orc_decode_sequence
+ *       the SDK's greedy paged decoder loop (attention_cuda.cu:754-1090:
+ *       RMSNorm, GEMVs, RoPE on q and the stored k, softmax attention,
+ *       SwiGLU, argmax), rounding to the storage type where the SDK does.
  *   orc_paged_attention
  *       gather a sequence's K/V through its block table, widen to FP32 with
  *       the conversions above, and run orc_sdpa_f32 on [1, Hkv, L, d] -- the
@@ -277,4 +281,174 @@ int orc_paged_attention_rows(const uint16_t *q_rows, const int64_t *q_pos, size_
     }
     free(kf); free(vf); free(qf); free(sc); free(of);
     return ok;
+}
+
+/* ------------------------------------------------------------------------
+ * orc_decode_sequence -- greedy decoding of one sequence through the SDK's
+ * dense decoder stack, restating decode_sequence_impl
+ * (attention_cuda.cu:754-1090) and its kernels on the CPU:
+ *   embedding row (:100-104); RMSNorm x * (1/sqrt(mean(x^2) + eps)) * w
+ *   (:106-124); GEMV with FP32 sums (:126-163; quantised Q8_0/Q4_0 blocks
+ *   :197-213, scale * q exactly); RoPE over split halves with angle
+ *   position / theta^(2f/d) applied to q and to the stored k, v stored as
+ *   is (:307-341); scores q.k * (1/sqrt(d)), softmax with the all-non-finite
+ *   rule and expf (:343-379), P.V (:381-398); o-projection + residual, the
+ *   quantised path rounding the product first (:293-299, :1040-1046);
+ *   SwiGLU g / (1 + expf(-g)) * u (:165-195); final norm, lm_head, first
+ *   strict argmax (:400-410).  Every value the SDK stores in T (float for
+ *   F32 storage, half otherwise) is rounded to T here at the same point.
+ *   Sums are sequential; the GPU's are tree-shaped, so the two agree to
+ *   FP32 rounding.
+ * storage 0 = F32, 1 = F16, 2 = quantised F16 (fmt 1 = Q8_0, 2 = Q4_0).
+ * layers: per layer 9 pointers (input_norm, q, k, v, o, post_norm, gate, up,
+ * down).  kcache/vcache: per layer [capacity][kv_width] in T, positions
+ * [0, past) hold the prefix; positions [past, past + count) are written.
+ * all_logits (optional, token_count * vocab floats): every step's logits.
+ * ------------------------------------------------------------------------ */
+static int dec_storage;
+static float dec_ld(const void *p, size_t i) {
+    return dec_storage == 0 ? ((const float *)p)[i] : orc_f16_to_f32(((const uint16_t *)p)[i]);
+}
+static float dec_rt(float v) { return dec_storage == 0 ? v : orc_f16_to_f32(orc_f32_to_f16(v)); }
+static void dec_st(void *p, size_t i, float v) {
+    if (dec_storage == 0) ((float *)p)[i] = v;
+    else ((uint16_t *)p)[i] = orc_f32_to_f16(v);
+}
+
+static void dec_rms(const float *x, const void *w, float *y, size_t n, float eps) {
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; ++i) sum = fmaf(x[i], x[i], sum);
+    const float scale = 1.0f / sqrtf(sum / (float)n + eps);
+    for (size_t i = 0; i < n; ++i) y[i] = dec_rt(x[i] * scale * dec_ld(w, i));
+}
+
+/* one row's FP32 sum */
+static float dec_dot(const void *m, int fmt, size_t row, const float *x, size_t in) {
+    float sum = 0.0f;
+    if (fmt == 0) {
+        for (size_t i = 0; i < in; ++i) sum = fmaf(x[i], dec_ld(m, row * in + i), sum);
+        return sum;
+    }
+    const size_t bb = fmt == 1 ? 34 : 18, nb = in / 32;
+    const uint8_t *w = (const uint8_t *)m + row * nb * bb;
+    for (size_t b = 0; b < nb; ++b) {
+        const uint8_t *blk = w + b * bb;
+        const float scale = orc_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+        for (size_t k = 0; k < 32; ++k) {
+            int q;
+            if (fmt == 1) q = (int)(int8_t)blk[2 + k];
+            else {
+                const uint8_t packed = blk[2 + (k & 15)];
+                q = (int)(k < 16 ? packed & 15 : packed >> 4) - 8;
+            }
+            sum = fmaf(x[b * 32 + k], scale * (float)q, sum);
+        }
+    }
+    return sum;
+}
+
+int orc_decode_sequence(int storage, int fmt, const void *const *layers, size_t layer_count,
+                        const void *embedding, uint32_t initial_token, size_t token_count,
+                        uint32_t *generated, void *const *kcache, void *const *vcache,
+                        size_t past, size_t capacity, size_t hidden, size_t inter, size_t qh,
+                        size_t kvh, size_t hd, float eps, double theta, const void *final_norm,
+                        const void *lm_head, size_t vocab, float *all_logits) {
+    if (storage < 0 || storage > 2 || qh * hd != hidden || qh % kvh || hd % 2 ||
+        past + token_count > capacity || (storage == 2 && fmt != 1 && fmt != 2))
+        return 0;
+    dec_storage = storage;
+    const int wf = storage == 2 ? fmt : 0;
+    const size_t kvw = kvh * hd, qkvw = hidden + 2 * kvw, group = qh / kvh;
+    float *x = malloc(hidden * 4), *n = malloc(hidden * 4), *qkv = malloc(qkvw * 4);
+    float *q = malloc(hidden * 4), *att = malloc(hidden * 4), *r = malloc(hidden * 4);
+    float *act = malloc(inter * 4), *logits = malloc(vocab * 4);
+    float *scores = malloc((past + token_count) * 4);
+    if (!x || !n || !qkv || !q || !att || !r || !act || !logits || !scores) return 0;
+    const float ftheta = (float)theta, scale = 1.0f / sqrtf((float)hd);
+    uint32_t token = initial_token;
+    for (size_t t = 0; t < token_count; ++t) {
+        const size_t pos = past + t, len = pos + 1;
+        for (size_t i = 0; i < hidden; ++i) x[i] = dec_ld(embedding, (size_t)token * hidden + i);
+        for (size_t l = 0; l < layer_count; ++l) {
+            const void *const *w = layers + 9 * l;
+            dec_rms(x, w[0], n, hidden, eps);
+            for (size_t o = 0; o < qkvw; ++o) {
+                const void *m = o < hidden ? w[1] : (o < hidden + kvw ? w[2] : w[3]);
+                const size_t row = o < hidden ? o : (o < hidden + kvw ? o - hidden : o - hidden - kvw);
+                qkv[o] = dec_rt(dec_dot(m, wf, row, n, hidden));
+            }
+            const size_t half = hd / 2;
+            for (size_t i = 0; i < (hidden > kvw ? hidden : kvw); ++i) {
+                const size_t dim = i % hd, base = i - dim;
+                const size_t paired = base + (dim < half ? dim + half : dim - half);
+                const size_t freq = dim < half ? dim : dim - half;
+                const float angle = (float)pos / powf(ftheta, 2.0f * (float)freq / (float)hd);
+                const float sign = dim < half ? -1.0f : 1.0f;
+                if (i < hidden) q[i] = dec_rt(qkv[i] * cosf(angle) + sign * qkv[paired] * sinf(angle));
+                if (i < kvw) {
+                    const float *k = qkv + hidden;
+                    dec_st(kcache[l], pos * kvw + i, k[i] * cosf(angle) + sign * k[paired] * sinf(angle));
+                    dec_st(vcache[l], pos * kvw + i, qkv[hidden + kvw + i]);
+                }
+            }
+            for (size_t h = 0; h < qh; ++h) {
+                const size_t g = h / group;
+                float mx = -INFINITY;
+                for (size_t p = 0; p < len; ++p) {
+                    float s = 0.0f;
+                    for (size_t d = 0; d < hd; ++d)
+                        s = fmaf(q[h * hd + d], dec_ld(kcache[l], p * kvw + g * hd + d), s);
+                    scores[p] = s * scale;
+                    mx = fmaxf(mx, scores[p]);
+                }
+                if (!isfinite(mx)) {
+                    for (size_t p = 0; p < len; ++p) scores[p] = 0.0f;
+                } else {
+                    float sum = 0.0f;
+                    for (size_t p = 0; p < len; ++p) {
+                        scores[p] = expf(scores[p] - mx);
+                        sum += scores[p];
+                    }
+                    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+                    for (size_t p = 0; p < len; ++p) scores[p] *= inv;
+                }
+                for (size_t d = 0; d < hd; ++d) {
+                    float s = 0.0f;
+                    for (size_t p = 0; p < len; ++p)
+                        s = fmaf(scores[p], dec_ld(vcache[l], p * kvw + g * hd + d), s);
+                    att[h * hd + d] = dec_rt(s);
+                }
+            }
+            for (size_t o = 0; o < hidden; ++o) {
+                float v = dec_dot(w[4], wf, o, att, hidden);
+                if (wf) v = dec_rt(v);
+                r[o] = dec_rt(v + x[o]);
+            }
+            dec_rms(r, w[5], n, hidden, eps);
+            for (size_t o = 0; o < inter; ++o) {
+                const float g = dec_dot(w[6], wf, o, n, hidden);
+                const float u = dec_dot(w[7], wf, o, n, hidden);
+                act[o] = dec_rt(g / (1.0f + expf(-g)) * u);
+            }
+            for (size_t o = 0; o < hidden; ++o) {
+                float v = dec_dot(w[8], wf, o, act, inter);
+                if (wf) v = dec_rt(v);
+                x[o] = dec_rt(v + r[o]);
+            }
+        }
+        dec_rms(x, final_norm, n, hidden, eps);
+        for (size_t o = 0; o < vocab; ++o) logits[o] = dec_rt(dec_dot(lm_head, wf, o, n, hidden));
+        size_t best = 0;
+        float maximum = logits[0];
+        for (size_t i = 1; i < vocab; ++i)
+            if (logits[i] > maximum) {
+                maximum = logits[i];
+                best = i;
+            }
+        token = (uint32_t)best;
+        generated[t] = token;
+        if (all_logits) memcpy(all_logits + t * vocab, logits, vocab * 4);
+    }
+    free(x); free(n); free(qkv); free(q); free(att); free(r); free(act); free(logits); free(scores);
+    return 1;
 }

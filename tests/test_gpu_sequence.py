@@ -1,0 +1,208 @@
+"""GPU parity of tensor_attention_decode_sequence_paged (include/attention.h)
+against the CPU restatement of the SDK's decoder loop (orc_decode_sequence)
+and, where it was built, the SDK's own CUDA backend run on the same inputs.
+
+Cases follow the SDK's own paged-decoder tests (test_attention.c:108-341):
+tiny F16 shapes, a decode split over two calls, a host prefix import, a
+1025-token prefix over 16-token pages, two sequences interleaved in one
+cache, a rejected shape that must leave the cache untouched, F32 storage,
+and Q8_0/Q4_0 weights; plus larger GQA models that run the tcgen05
+(head_dim 128) and CUDA-core (head_dim 64) paged decode kernels, with the
+pages they wrote compared to the oracle's cache."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import inference_c_b200 as P
+from oracle import oracle as O
+from tests.decoder_cases import Model, assert_tokens_agree
+from tests.gpu_cases import check_close
+
+pytestmark = pytest.mark.gpu
+
+EPS, THETA = 1e-5, 10000.0
+
+
+def ours(m: Model, cache, seq, initial, count, kc, vc, past):
+    return P.decode_sequence_paged(cache, seq, m.storage, m.layer_tensors(), m.embedding_s(),
+                                   initial, count, kc, vc, past, m.hidden, m.inter, m.qh, m.kvh,
+                                   m.hd, EPS, THETA, m.final_norm_s(), m.lm_head_s(), m.vocab,
+                                   m.fmt)
+
+
+def empty_cache(m: Model, cap: int):
+    z = np.zeros((cap, m.kvw), m.cache_dtype())
+    return [z.copy() for _ in range(m.n_layers)], [z.copy() for _ in range(m.n_layers)]
+
+
+def ref_tokens(m: Model, block, blocks, initial, count, kc, vc, past):
+    if not O.ref_cuda_available():
+        return None
+    r = O.RefCudaDecoder(block, blocks)
+    try:
+        return r.decode(m.storage, m.fmt, m.layer_tensors(), m.embedding_s(), initial, count, kc,
+                        vc, past, m.hidden, m.inter, m.qh, m.kvh, m.hd, EPS, THETA,
+                        m.final_norm_s(), m.lm_head_s(), m.vocab)
+    finally:
+        r.close()
+
+
+@pytest.fixture(autouse=True)
+def _clear(lib, cuda):
+    yield
+    P.decode_cache_clear()
+
+
+@pytest.mark.parametrize("kind", ["f16", "f32"])
+def test_tiny_model_and_split_calls(oracle_mod, kind):
+    m = Model(kind, 1, 4, 8, 2, 2, 2, 16, seed=11)
+    cap, block = 16, 2
+    kc, vc = empty_cache(m, cap)
+    want, logits, _, _ = m.oracle(oracle_mod, 1, 6, kc, vc, 0, cap)
+    cache = P.PagedKVCache(block, cap // block, 1)
+    seq = cache.sequence_create()
+    got = ours(m, cache, seq, 1, 6, kc, vc, 0)
+    assert_tokens_agree(got, want, logits, "one call")
+    assert cache.length(seq) == 6 and cache.free_blocks() == cap // block - 3
+    # the same decode in two calls
+    cache2 = P.PagedKVCache(block, cap // block, 1)
+    s2 = cache2.sequence_create()
+    a = ours(m, cache2, s2, 1, 3, kc, vc, 0)
+    b = ours(m, cache2, s2, a[-1], 3, kc, vc, 3)
+    assert_tokens_agree(a + b, want, logits, "two calls")
+    ref = ref_tokens(m, block, cap // block, 1, 6, kc, vc, 0)
+    if ref is not None:
+        assert_tokens_agree(got, ref, logits, "SDK CUDA backend")
+    assert cache.release(seq) and cache.free_blocks() == cap // block
+    cache.free()
+    cache2.free()
+
+
+def test_prefix_import_and_rejected_shape(oracle_mod):
+    m = Model("f16", 1, 4, 8, 2, 2, 2, 16, seed=12)
+    cap, block = 16, 2
+    kc, vc = m.prefix(3, cap, seed=5)
+    want, logits, _, _ = m.oracle(oracle_mod, 1, 2, kc, vc, 3, cap)
+    cache = P.PagedKVCache(block, cap // block, 1)
+    seq = cache.sequence_create()
+    bad = P.decode_sequence_paged(cache, seq, m.storage, m.layer_tensors(), m.embedding_s(), 1,
+                                  2, kc, vc, 3, m.hidden, m.inter, m.qh, m.kvh, 4, EPS, THETA,
+                                  m.final_norm_s(), m.lm_head_s(), m.vocab)
+    assert bad is None and cache.free_blocks() == cap // block and cache.length(seq) == 0
+    got = ours(m, cache, seq, 1, 2, kc, vc, 3)
+    assert_tokens_agree(got, want, logits, "prefix import")
+    assert cache.length(seq) == 5 and cache.free_blocks() == cap // block - 3
+    # a wrong past length for a sequence that already holds tokens is refused
+    assert ours(m, cache, seq, got[-1], 1, kc, vc, 4) is None and cache.length(seq) == 5
+    ref = ref_tokens(m, block, cap // block, 1, 2, kc, vc, 3)
+    if ref is not None:
+        assert_tokens_agree(got, ref, logits, "SDK CUDA backend")
+    cache.free()
+
+
+def test_long_prefix_over_16_token_pages(oracle_mod):
+    m = Model("f16", 1, 4, 8, 2, 2, 2, 16, seed=13)
+    past, cap, block = 1025, 1040, 16
+    kc, vc = m.prefix(past, cap, seed=6)
+    want, logits, _, _ = m.oracle(oracle_mod, 1, 1, kc, vc, past, cap)
+    cache = P.PagedKVCache(block, cap // block, 1)
+    seq = cache.sequence_create()
+    got = ours(m, cache, seq, 1, 1, kc, vc, past)
+    assert_tokens_agree(got, want, logits, "1025-token prefix")
+    ref = ref_tokens(m, block, cap // block, 1, 1, kc, vc, past)
+    if ref is not None:
+        assert_tokens_agree(got, ref, logits, "SDK CUDA backend")
+    cache.free()
+
+
+def test_two_sequences_interleaved(oracle_mod):
+    m = Model("f16", 1, 4, 8, 2, 2, 2, 16, seed=14)
+    cap, block = 8, 2
+    kc, vc = empty_cache(m, cap)
+    want_a, la, _, _ = m.oracle(oracle_mod, 1, 2, kc, vc, 0, cap)
+    want_b, lb, _, _ = m.oracle(oracle_mod, 2, 2, kc, vc, 0, cap)
+    cache = P.PagedKVCache(block, 4, 2)
+    sa, sb = cache.sequence_create(), cache.sequence_create()
+    a0 = ours(m, cache, sa, 1, 1, kc, vc, 0)
+    b0 = ours(m, cache, sb, 2, 1, kc, vc, 0)
+    a1 = ours(m, cache, sa, a0[0], 1, kc, vc, 1)
+    b1 = ours(m, cache, sb, b0[0], 1, kc, vc, 1)
+    assert_tokens_agree(a0 + a1, want_a, la, "sequence a")
+    assert_tokens_agree(b0 + b1, want_b, lb, "sequence b")
+    assert cache.release(sa) and cache.release(sb) and cache.free_blocks() == 4
+    cache.free()
+
+
+@pytest.mark.parametrize("kind", ["q8", "q4", "f32"])
+def test_storage_kinds(oracle_mod, kind):
+    m = Model(kind, 2, 64, 96, 4, 2, 16, 48, seed=15)
+    cap, block = 32, 4
+    kc, vc = m.prefix(5, cap, seed=7)
+    want, logits, _, _ = m.oracle(oracle_mod, 3, 5, kc, vc, 5, cap)
+    cache = P.PagedKVCache(block, cap // block, 1)
+    seq = cache.sequence_create()
+    got = ours(m, cache, seq, 3, 5, kc, vc, 5)
+    assert_tokens_agree(got, want, logits, kind)
+    ref = ref_tokens(m, block, cap // block, 3, 5, kc, vc, 5)
+    if ref is not None:
+        assert_tokens_agree(got, ref, logits, f"SDK CUDA backend {kind}")
+    cache.free()
+
+
+def gathered_pages(cache, seq, layer, m: Model, length: int):
+    """K and V rows 0..length-1 of one sequence, read back through the pool
+    with pkv_kv_gather (float32 arrays)."""
+    import ctypes
+    import torch
+    from tests.gpu_cases import to_host_bits
+    lib = P.load()
+    pool = lib.pkv_pool_from_cache(cache.handle)
+    pl = P.PkvPagedLayer()
+    assert lib.pkv_pool_layer(pool, layer, ctypes.byref(pl))
+    table = np.array(cache.block_table(seq), dtype=np.uint32)
+    d_tab = torch.from_numpy(table.view(np.int32)).cuda().view(1, -1)
+    d_len = torch.tensor([length], dtype=torch.int32, device="cuda")
+    offs = torch.tensor([0, length], dtype=torch.int32, device="cuda")
+    k = torch.empty(length, m.kvw, dtype=torch.float16, device="cuda")
+    v = torch.empty_like(k)
+    P.kv_gather(pl, P.make_batch(d_tab, d_len), k, v, offs.data_ptr())
+    torch.cuda.synchronize()
+    f = lambda t: to_host_bits(t).view(np.float16).astype(np.float32)
+    return f(k), f(v)
+
+
+@pytest.mark.parametrize("hd,qh,kvh", [(128, 8, 2), (64, 8, 4)])
+def test_fast_attention_paths_and_pages(oracle_mod, hd, qh, kvh):
+    """Head_dim 128 runs the tcgen05 paged decode, 64 the CUDA-core one."""
+    m = Model("f16", 2, qh * hd, 1536, qh, kvh, hd, 512, seed=16 + hd)
+    past, count, cap, block = 300, 4, 320, 16
+    kc, vc = m.prefix(past, cap, seed=8)
+    want, logits, okc, ovc = m.oracle(oracle_mod, 7, count, kc, vc, past, cap)
+    cache = P.PagedKVCache(block, cap // block, 1)
+    seq = cache.sequence_create()
+    got = ours(m, cache, seq, 7, count, kc, vc, past)
+    agree = assert_tokens_agree(got, want, logits, f"head_dim {hd}")
+    length = past + count
+    f = lambda a: a.view(np.float16).astype(np.float32)
+    for layer in range(m.n_layers):
+        k, v = gathered_pages(cache, seq, layer, m, length)
+        assert np.array_equal(k[:past], f(kc[layer][:past]))  # prefix import: bit copies
+        assert np.array_equal(v[:past], f(vc[layer][:past]))
+        n = past + min(agree, count)  # rows written before any near-tie divergence
+        if layer == 0:
+            # inputs identical to the oracle's (embedding rows): element tolerance
+            check_close(k[past:n], f(okc[layer][past:n]), f"K rows layer {layer}")
+            check_close(v[past:n], f(ovc[layer][past:n]), f"V rows layer {layer}")
+        else:
+            # after a layer of FP16-rounded activations the two paths' last-bit
+            # differences compound: compare whole rows relative to their norm
+            for got_rows, want_rows in ((k, okc), (v, ovc)):
+                want_f = f(want_rows[layer][past:n])
+                err = np.linalg.norm(got_rows[past:n] - want_f) / np.linalg.norm(want_f)
+                assert err <= 1e-2, f"layer {layer} rows: relative error {err:.2e}"
+    ref = ref_tokens(m, block, cap // block, 7, count, kc, vc, past)
+    if ref is not None:
+        assert_tokens_agree(got, ref, logits, "SDK CUDA backend")
+    assert P.device_fault(0) == 0
+    cache.free()
