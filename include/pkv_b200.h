@@ -58,8 +58,8 @@ typedef struct {
     size_t block_size;  /* tokens per page */
     size_t block_count; /* pages in the pool (device bounds checks use it) */
     size_t kv_heads;
-    size_t head_dim;    /* 64 or 128 */
-    PkvDType dtype;     /* storage: F16 or BF16 */
+    size_t head_dim;    /* kernels: 64 or 128 */
+    PkvDType dtype;     /* storage: F16 or BF16 (F32 pools serve only the decoder entry point) */
 } PkvPagedLayer;
 
 /* The sequences of one batch, as the kernels see them (device pointers). */
@@ -179,7 +179,8 @@ typedef struct PkvPool PkvPool;
  * a padded device block table for up to max_batch sequences of up to
  * max_pages_per_seq pages, and attaches the pool to the cache as its CUDA
  * backend state (tensor_paged_kv_cache_free destroys it).  Pools start
- * zeroed.  Replaces get_cuda_paged_kv_state (attention_cuda.cu:570-612). */
+ * zeroed.  dtype F16 or BF16 (F32 for the decoder entry point of
+ * attention.h).  Replaces get_cuda_paged_kv_state (attention_cuda.cu:570-612). */
 int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
                     size_t layer_count, size_t kv_heads, size_t head_dim,
                     size_t max_batch, size_t max_pages_per_seq,
