@@ -35,6 +35,7 @@ import statistics
 import sys
 import threading
 import time
+import time
 
 import numpy as np
 
@@ -52,7 +53,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3)
+    p.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=3)
     p.add_argument("--chunk", type=int, default=0, help="decode split size in tokens (0: auto)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -852,15 +853,184 @@ def run_cfg4(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Config 6: the SDK's paged decoder entry point end to end
+# ---------------------------------------------------------------------------
+
+CFG6 = dict(layers=4, hidden=4096, inter=14336, qh=32, kvh=8, hd=128, vocab=32000,
+            context=4096, tokens=16, block=16)
+
+
+def cfg6_block() -> dict:
+    c = CFG6
+    return {"workload": ("cfg6: Llama-3-8B-shaped decoder, 4 of its 32 layers, F16 weights, "
+                         "GQA 32/8, d=128, vocab 32000, 4096-token context; a step = one "
+                         "tensor_attention_decode_sequence_paged call generating 16 tokens"),
+            **c, "storage": "TENSOR_PAGED_KV_F16", "weights": "host arrays, device copies "
+            "cached after the first call (as the SDK's CUDA backend)",
+            "l2": "no flush needed: each token streams 2.0 GB of weights (> 126 MB L2)"}
+
+
+def cfg6_model(seed: int):
+    """Seeded F16 weights (host, uint16 bits) and a 4096-token prefix."""
+    import torch
+    c = CFG6
+    g = torch.Generator().manual_seed(seed)
+    kvw = c["kvh"] * c["hd"]
+
+    def mat(o, i, gain=1.0):
+        return (torch.randn(o, i, generator=g) * (gain / i ** 0.5)).half().numpy().view(np.uint16)
+
+    def vec(n):
+        return (1 + 0.1 * torch.randn(n, generator=g)).half().numpy().view(np.uint16)
+
+    h, it = c["hidden"], c["inter"]
+    layers = [[vec(h), mat(h, h), mat(kvw, h), mat(kvw, h), mat(h, h, 0.5), vec(h), mat(it, h),
+               mat(it, h), mat(h, it, 0.5)] for _ in range(c["layers"])]
+    emb = torch.randn(c["vocab"], h, generator=g).half().numpy().view(np.uint16)
+    head = mat(c["vocab"], h, 4.0)
+    cap = c["context"] + c["tokens"] * 64
+    kc = [torch.randn(cap, kvw, generator=g).half().numpy().view(np.uint16)
+          for _ in range(c["layers"])]
+    vc = [torch.randn(cap, kvw, generator=g).half().numpy().view(np.uint16)
+          for _ in range(c["layers"])]
+    return layers, emb, vec(h), head, kc, vc, cap
+
+
+def cfg6_bytes_per_token(context: int) -> float:
+    """Weight bytes every token streams (all layer matrices and norms, lm_head,
+    one embedding row) plus the visible K/V rows of every layer."""
+    c = CFG6
+    h, it, kvw = c["hidden"], c["inter"], c["kvh"] * c["hd"]
+    layer = 2 * (h * h + 2 * kvw * h + h * h + 3 * it * h + 2 * h)
+    return c["layers"] * (layer + context * kvw * 2 * 2) + 2 * c["vocab"] * h + 2 * h
+
+
+def run_decoder(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # one sequence: a single-GPU configuration
+    import torch
+    c = CFG6
+    torch.cuda.set_device(0)
+    layers, emb, fnorm, head, kc, vc, cap = cfg6_model(args.seed)
+    steps, warmup = args.steps, args.warmup
+    pages = (cap + c["block"] - 1) // c["block"]
+    ref = args.impl == "reference"
+    if ref:
+        from oracle import oracle as O
+        if not O.ref_cuda_available():
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "oracle/_ref/libref_cuda.so (the SDK's CUDA backend) not built"}))
+            return
+        dec = O.RefCudaDecoder(c["block"], pages)
+
+        def call(initial, count, past):
+            return dec.decode(1, 0, layers, emb, initial, count, kc, vc, past, c["hidden"],
+                              c["inter"], c["qh"], c["kvh"], c["hd"], 1e-5, 500000.0, fnorm,
+                              head, c["vocab"])
+    else:
+        import inference_c_b200 as P
+        P.load()
+        cache = P.PagedKVCache(c["block"], pages, 1)
+        seq = cache.sequence_create()
+
+        def call(initial, count, past):
+            return P.decode_sequence_paged(cache, seq, P.TENSOR_PAGED_KV_F16, layers, emb,
+                                           initial, count, kc, vc, past, c["hidden"], c["inter"],
+                                           c["qh"], c["kvh"], c["hd"], 1e-5, 500000.0, fnorm,
+                                           head, c["vocab"])
+    # first call: prefix import of the 4096-token context and weight upload (untimed)
+    past = c["context"]
+    toks = call(1, 1, past)
+    assert toks is not None, "decoder call failed"
+    past += 1
+    token = toks[-1]
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(0).uuid))
+    times = []
+    with sampler:
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            toks = call(token, c["tokens"], past)
+            dt = time.perf_counter() - t0
+            assert toks is not None, "decoder call failed"
+            token, past = toks[-1], past + c["tokens"]
+            if i >= warmup:
+                times.append(dt)
+    ms = statistics.mean(times) * 1e3
+    tps = c["tokens"] / (ms / 1e3)
+    mid_context = c["context"] + 1 + c["tokens"] * (warmup + steps / 2)
+    bpt = cfg6_bytes_per_token(int(mid_context))
+    hbm, hbm_kind = peak_hbm()
+    gbs = bpt * tps / 1e9
+    line = {
+        "metric": "paged decoder tokens/s (config 6: tensor_attention_decode_sequence_paged, "
+                  "16 greedy tokens per call)",
+        "value": tps, "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic: seeded N(0,1)-scaled F16 weights and context",
+        "config": cfg6_block(),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "traffic": None, "peak_kind": hbm_kind,
+                     "bytes_per_token": bpt,
+                     "note": "whole call timed on the host clock (the API is synchronous): "
+                             "weights + visible K/V per token over the call time"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * c["tokens"],
+                "api": "tensor_attention_decode_sequence_paged (host token in, host tokens out)"},
+        "gpu_launches": None,
+        "clocks": sampler.summary(),
+    }
+    if ref:
+        line["impl"] = "reference"
+        line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0,
+                                "kind": "reference",
+                                "sample": "the SDK's own CUDA backend (attention_cuda.cu) built "
+                                          "from its sources, on the same GPU; the SDK has no CPU "
+                                          "decoder"}
+        dec.close()
+    else:
+        line["gpu_launches"] = c["tokens"] * (9 * c["layers"] + 3) * steps
+        cache.free()
+    print(json.dumps(line), flush=True)
+
+
+def run_prefill_reference(args) -> None:
+    """--impl reference for config 5: the SDK's tensor_sdpa_f32 on a bounded
+    slice of the workload each step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps, warmup = args.steps, args.warmup
+    budget = max(0.05, 150.0 / max(1, steps + warmup))
+    rates, info = [], None
+    for i in range(warmup + steps):
+        r, info = sdk_prefill_rate(budget, args.seed)
+        if i >= warmup:
+            rates.append(r)
+    value = statistics.mean(rates)
+    print(json.dumps({
+        "metric": "chunked prefill attention TFLOP/s over the paged cache (config 5: append "
+                  "2048-token chunks + causal prefill per step)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps,
+        "warmup": warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) BF16)",
+        "impl": "reference", "config": cfg5_block(),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", **info},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def main():
     args = parse_args()
-    if args.config == 4:
-        run_cfg4(args)
-        return
-    if args.config == 5:
-        run_prefill(args)
+    if args.config == 6:
+        run_decoder(args)
+    elif args.config == 5:
+        run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.config == 4:
+        run_cfg4(args)
     else:
         run_ours(args)
 
