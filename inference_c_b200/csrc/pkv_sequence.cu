@@ -56,7 +56,8 @@ __device__ uint32_t g_sequence_fault;
 constexpr int kGemvThreads = 256;
 constexpr int kAttnThreads = 256;
 constexpr int kAttnChunk = 512;   // positions per split of the generic attention
-constexpr int kArgmaxThreads = 1024;
+constexpr int kGemvMaxGrid = 148 * 16;
+constexpr int kGemvMaxIn = 53248;  // input elements staged in shared memory (208 KiB)
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -73,16 +74,26 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 
 // ---------------------------------------------------------------- GEMV ----
 enum class WF : int { Dense = 0, Q8 = 1, Q4 = 2 };
-enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2 };
+enum Epi : int { kPlain = 0, kResidual = 1, kSwiGLU = 2, kArgmax = 3 };
 
 struct GemvArgs {
     const void *m[3];  // matrices; output rows stack m[0], m[1], m[2] (SwiGLU: gate, up)
     int rows[3];
     int in;
     int out;
-    const void *x;
-    const void *res;
-    void *y;
+    const void *x;       // input vector (T)
+    const void *norm_w;  // RMSNorm weight applied to x first (nullptr: none)
+    float eps;
+    const void *res;     // residual (T) for kResidual
+    void *y;             // output (T)
+    // kArgmax: per-CTA best (value, index), ticket, outputs
+    float *part_v;
+    int *part_i;
+    unsigned *ticket;
+    uint32_t *tokens;      // outputs, indexed by *step
+    uint32_t *next_token;  // the next step's input token
+    int32_t *step;         // tokens generated so far in this call
+    int32_t *position;     // position of the next token
 };
 
 // One element of a Q*_0 block (scale * q, exact in FP32).
@@ -93,9 +104,28 @@ __device__ __forceinline__ float quant_value(const uint8_t *block, float scale, 
     return scale * (float)((int)(k < 16 ? packed & 15 : packed >> 4) - 8);
 }
 
-// Dot product of one matrix row with x, summed over the warp's lanes.
-template <typename T, WF F>
-__device__ __forceinline__ float row_dot(const void *mat, int row, int in, const T *x, int lane) {
+// E input elements starting at element i: from shared memory (FP32) or from
+// global memory (T, one 16-byte load when E elements fill it).
+template <typename T, int E>
+__device__ __forceinline__ void load_x(const float *xs, int i, float (&v)[E]) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = xs[i + e];
+}
+template <typename T, int E>
+__device__ __forceinline__ void load_x(const T *x, int i, float (&v)[E]) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(x + i));
+    const T *t = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = to_f(t[e]);
+}
+__device__ __forceinline__ float load_x1(const float *xs, int i) { return xs[i]; }
+template <typename T>
+__device__ __forceinline__ float load_x1(const T *x, int i) { return to_f(x[i]); }
+
+// Dot product of one matrix row with the input vector (XT: FP32 staged in
+// shared memory, or T read from global memory), summed over the warp.
+template <typename T, WF F, typename XT>
+__device__ __forceinline__ float row_dot(const void *mat, int row, int in, const XT *x, int lane) {
     float acc = 0.f;
     if (F == WF::Dense) {
         const T *w = static_cast<const T *>(mat) + (size_t)row * in;
@@ -105,32 +135,32 @@ __device__ __forceinline__ float row_dot(const void *mat, int row, int in, const
         if (vec) {
             const int nv = in / E;
             const uint4 *wv = reinterpret_cast<const uint4 *>(w);
-            const uint4 *xv = reinterpret_cast<const uint4 *>(x);
             int c = lane;
-            for (; c + 96 < nv; c += 128) {  // four 16-byte loads in flight per lane
-                uint4 a[4], b[4];
+            for (; c + 96 < nv; c += 128) {  // four 16-byte weight loads in flight per lane
+                uint4 a[4];
+                float xv[4][E];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     a[u] = __ldg(wv + c + 32 * u);
-                    b[u] = __ldg(xv + c + 32 * u);
+                    load_x<T, E>(x, (c + 32 * u) * E, xv[u]);
                 }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const T *wa = reinterpret_cast<const T *>(&a[u]);
-                    const T *xb = reinterpret_cast<const T *>(&b[u]);
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc = fmaf(to_f(xb[e]), to_f(wa[e]), acc);
+                    for (int e = 0; e < E; ++e) acc = fmaf(xv[u][e], to_f(wa[e]), acc);
                 }
             }
             for (; c < nv; c += 32) {
-                const uint4 a = __ldg(wv + c), b = __ldg(xv + c);
+                const uint4 a = __ldg(wv + c);
+                float xv[E];
+                load_x<T, E>(x, c * E, xv);
                 const T *wa = reinterpret_cast<const T *>(&a);
-                const T *xb = reinterpret_cast<const T *>(&b);
 #pragma unroll
-                for (int e = 0; e < E; ++e) acc = fmaf(to_f(xb[e]), to_f(wa[e]), acc);
+                for (int e = 0; e < E; ++e) acc = fmaf(xv[e], to_f(wa[e]), acc);
             }
         } else {
-            for (int i = lane; i < in; i += 32) acc = fmaf(to_f(x[i]), to_f(w[i]), acc);
+            for (int i = lane; i < in; i += 32) acc = fmaf(load_x1(x, i), to_f(w[i]), acc);
         }
     } else {
         constexpr int BB = F == WF::Q8 ? 34 : 18;
@@ -140,39 +170,128 @@ __device__ __forceinline__ float row_dot(const void *mat, int row, int in, const
             const uint8_t *blk = w + (size_t)b * BB;
             const uint16_t bits = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
             const float scale = __half2float(__ushort_as_half(bits));
-            const T *xb = x + b * 32;
 #pragma unroll 8
-            for (int k = 0; k < 32; ++k) acc = fmaf(to_f(xb[k]), quant_value<F>(blk, scale, k), acc);
+            for (int k = 0; k < 32; ++k)
+                acc = fmaf(load_x1(x, b * 32 + k), quant_value<F>(blk, scale, k), acc);
         }
     }
     return warp_sum_f(acc);
 }
 
-template <typename T, WF F, int EPI>
+// First maximum merge: (v, i) replaces (bv, bi) when strictly larger, or
+// equal with a smaller index.  NaN never wins.
+__device__ __forceinline__ void best_merge(float &bv, int &bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+// y[r] = epilogue(M[r] . n), n = x, or RMSNorm(x) rounded to T as the SDK
+// stores it, then staged once per CTA in shared memory as FP32.  One warp
+// per output row; the CTAs stride over the rows.
+template <typename T, WF F, int EPI, bool NORM>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
-    const int lane = threadIdx.x & 31;
+    extern __shared__ float xs[];
+    __shared__ float red[kGemvThreads / 32];
+    __shared__ int redi[kGemvThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int warps = kGemvThreads / 32;
     const T *x = static_cast<const T *>(a.x);
+    if (NORM) {
+        // RMSNorm (attention_cuda.cu:106-124): x * rsqrt(mean(x^2) + eps) * w
+        float s = 0.f;
+        for (int i = threadIdx.x; i < a.in; i += kGemvThreads) {
+            const float v = to_f(x[i]);
+            s = fmaf(v, v, s);
+        }
+        s = warp_sum_f(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < warps; ++w) tot += red[w];
+        const float scale = rsqrtf(tot / (float)a.in + a.eps);
+        const T *nw = static_cast<const T *>(a.norm_w);
+        for (int i = threadIdx.x; i < a.in; i += kGemvThreads)
+            xs[i] = to_f(from_f32<T>(to_f(x[i]) * scale * to_f(nw[i])));
+        __syncthreads();
+    }
     T *y = static_cast<T *>(a.y);
-    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < a.out; r += gridDim.x * warps) {
+    float bv = -INFINITY;
+    int bi = INT32_MAX;
+    for (int r = blockIdx.x * warps + warp; r < a.out; r += gridDim.x * warps) {
         if (EPI == kSwiGLU) {
-            const float g = row_dot<T, F>(a.m[0], r, a.in, x, lane);
-            const float u = row_dot<T, F>(a.m[1], r, a.in, x, lane);
+            const float g = NORM ? row_dot<T, F>(a.m[0], r, a.in, xs, lane)
+                                 : row_dot<T, F>(a.m[0], r, a.in, x, lane);
+            const float u = NORM ? row_dot<T, F>(a.m[1], r, a.in, xs, lane)
+                                 : row_dot<T, F>(a.m[1], r, a.in, x, lane);
             if (lane == 0) y[r] = from_f32<T>(g / (1.0f + expf(-g)) * u);
             continue;
         }
         int mi = 0, rr = r;
         while (mi < 2 && rr >= a.rows[mi]) rr -= a.rows[mi++];
-        const float s = row_dot<T, F>(a.m[mi], rr, a.in, x, lane);
-        if (lane != 0) continue;
+        const float s = NORM ? row_dot<T, F>(a.m[mi], rr, a.in, xs, lane)
+                             : row_dot<T, F>(a.m[mi], rr, a.in, x, lane);
         if (EPI == kResidual) {
-            const float res = to_f(static_cast<const T *>(a.res)[r]);
-            // the quantised path rounds the product before the residual add
-            const float v = F == WF::Dense ? s : to_f(from_f32<T>(s));
-            y[r] = from_f32<T>(v + res);
+            if (lane == 0) {
+                const float res = to_f(static_cast<const T *>(a.res)[r]);
+                // the quantised path rounds the product before the residual add
+                const float v = F == WF::Dense ? s : to_f(from_f32<T>(s));
+                y[r] = from_f32<T>(v + res);
+            }
         } else {
-            y[r] = from_f32<T>(s);
+            const T t = from_f32<T>(s);
+            if (lane == 0) y[r] = t;
+            if (EPI == kArgmax) {
+                const float v = to_f(t);
+                if (v == v) best_merge(bv, bi, v, r);
+            }
         }
+    }
+    if (EPI != kArgmax) return;
+    // first argmax over all CTAs (attention_cuda.cu:400-410): per-CTA best,
+    // then the last CTA to finish reduces them
+    __shared__ int last;
+    if (lane == 0) {
+        red[warp] = bv;
+        redi[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < warps; ++w) best_merge(bv, bi, red[w], redi[w]);
+        a.part_v[blockIdx.x] = bv;
+        a.part_i[blockIdx.x] = bi;
+        __threadfence();
+        last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = INT32_MAX;
+    for (int c = threadIdx.x; c < (int)gridDim.x; c += kGemvThreads)
+        best_merge(bv, bi, __ldcg(a.part_v + c), __ldcg(a.part_i + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        best_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    if (lane == 0) {
+        red[warp] = bv;
+        redi[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < warps; ++w) best_merge(bv, bi, red[w], redi[w]);
+        // logits[0] starts the SDK's scan: a NaN there keeps index 0, and only
+        // a strictly larger value replaces it
+        const float first = to_f(__ldcg(static_cast<const T *>(a.y)));
+        const uint32_t t =
+            (first != first || bi == INT32_MAX || !(bv > first)) ? 0u : (uint32_t)bi;
+        a.tokens[*a.step] = t;
+        *a.next_token = t;
+        *a.step += 1;
+        *a.position += 1;
+        *a.ticket = 0u;
     }
 }
 
@@ -189,38 +308,18 @@ __global__ void embed_kernel(const T *emb, const uint32_t *token, T *x, int widt
         x[i] = emb[(size_t)t * width + i];
 }
 
-template <typename T>
-__global__ void __launch_bounds__(1024) rms_kernel(const T *x, const T *w, T *y, int width,
-                                                   float eps) {
-    __shared__ float part[32];
-    float s = 0.f;
-    for (int i = threadIdx.x; i < width; i += blockDim.x) {
-        const float v = to_f(x[i]);
-        s = fmaf(v, v, s);
-    }
-    s = warp_sum_f(s);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
-        t = warp_sum_f(t);
-        if (threadIdx.x == 0) part[0] = t;
-    }
-    __syncthreads();
-    const float scale = rsqrtf(part[0] / (float)width + eps);
-    for (int i = threadIdx.x; i < width; i += blockDim.x)
-        y[i] = from_f32<T>(to_f(x[i]) * scale * to_f(w[i]));
-}
-
 // RoPE of q (into qrot) and of the new k, k and v stored in their page row,
-// and the visible length position + 1 for the attention that follows.
+// and the visible length position + 1 for the attention that follows.  The
+// position lives on the device (advanced by the argmax), so one token's
+// launches are the same every step and replay as a CUDA graph.
 template <typename T>
 __global__ void rope_store_kernel(const T *qkv, T *qrot, T *kpool, T *vpool,
                                   const uint32_t *table, int table_stride, int block_size,
                                   uint32_t block_count, int hidden, int kv_width, int head_dim,
-                                  int position, float theta, int32_t *seq_len) {
+                                  const int32_t *position_dev, float theta, int32_t *seq_len) {
     const int index = blockIdx.x * blockDim.x + threadIdx.x;
     const int half_dim = head_dim / 2;
+    const int position = *position_dev;
     if (index == 0) *seq_len = position + 1;
     auto rotate = [&](const T *v, int i) -> float {
         const int dim = i % head_dim;
@@ -373,52 +472,6 @@ __global__ void attn_merge_kernel(const float *part, int splits, int head_dim, T
     }
 }
 
-// First maximum, as the SDK's sequential scan (attention_cuda.cu:400-410):
-// logits[0] starts the scan, only a strictly larger value replaces it, so a
-// NaN never wins and a NaN first element keeps index 0.
-template <typename T>
-__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T *logits, int vocab,
-                                                                uint32_t *token_out,
-                                                                uint32_t *next_token) {
-    __shared__ float sv[kArgmaxThreads / 32];
-    __shared__ int si[kArgmaxThreads / 32];
-    float bv = -INFINITY;
-    int bi = INT32_MAX;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-        const float v = to_f(logits[i]);
-        if (v == v && (v > bv || (v == bv && i < bi))) {
-            bv = v;
-            bi = i;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        sv[threadIdx.x >> 5] = bv;
-        si[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < kArgmaxThreads / 32; ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
-        const float first = to_f(logits[0]);
-        // index 0 when logits[0] is NaN or nothing beats it
-        const uint32_t t = (first != first || bi == INT32_MAX || !(bv > first)) ? 0u : (uint32_t)bi;
-        *token_out = t;
-        *next_token = t;
-    }
-}
-
 // ------------------------------------------------------------ host -------
 struct DevWeight {
     void *ptr = nullptr;
@@ -497,42 +550,83 @@ struct Dims {
     float eps, theta;
 };
 
-template <typename T, WF F, int EPI>
-bool launch_gemv(const GemvArgs &a, cudaStream_t s) {
+template <typename T, WF F, int EPI, bool NORM>
+bool launch_gemv_n(const GemvArgs &a, cudaStream_t s) {
     const int warps = kGemvThreads / 32;
     int grid = (a.out + warps - 1) / warps;
-    if (grid > 148 * 16) grid = 148 * 16;
-    gemv_kernel<T, F, EPI><<<grid, kGemvThreads, 0, s>>>(a);
+    if (grid > kGemvMaxGrid) grid = kGemvMaxGrid;
+    const size_t smem = NORM ? (size_t)a.in * sizeof(float) : 0;
+    static bool configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(gemv_kernel<T, F, EPI, NORM>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(kGemvMaxIn * sizeof(float))) != cudaSuccess)
+            return false;
+        configured[dev] = true;
+    }
+    gemv_kernel<T, F, EPI, NORM><<<grid, kGemvThreads, smem, s>>>(a);
     return cudaGetLastError() == cudaSuccess;
 }
 
+template <typename T, WF F, int EPI>
+bool launch_gemv(const GemvArgs &a, cudaStream_t s) {
+    return a.norm_w != nullptr ? launch_gemv_n<T, F, EPI, true>(a, s)
+                               : launch_gemv_n<T, F, EPI, false>(a, s);
+}
+
+// One matrix-vector product of the decoder.
+struct Gemv {
+    const void *m0 = nullptr, *m1 = nullptr, *m2 = nullptr;
+    int r0 = 0, r1 = 0, r2 = 0, in = 0, out = 0;
+    const void *x = nullptr, *norm_w = nullptr, *res = nullptr;
+    void *y = nullptr;
+    float eps = 0.f;
+    int epi = kPlain;
+    float *part_v = nullptr;
+    int *part_i = nullptr;
+    unsigned *ticket = nullptr;
+    uint32_t *tokens = nullptr, *next_token = nullptr;
+    int32_t *step = nullptr, *position = nullptr;
+};
+
 template <typename T, WF F>
-bool gemv(const void *m0, int r0, const void *m1, int r1, const void *m2, int r2, int in,
-          int out, const void *x, const void *res, void *y, int epi, cudaStream_t s) {
+bool run_gemv_f(const Gemv &g, cudaStream_t s) {
     GemvArgs a;
-    a.m[0] = m0;
-    a.m[1] = m1;
-    a.m[2] = m2;
-    a.rows[0] = r0;
-    a.rows[1] = r1;
-    a.rows[2] = r2;
-    a.in = in;
-    a.out = out;
-    a.x = x;
-    a.res = res;
-    a.y = y;
-    if (epi == kResidual) return launch_gemv<T, F, kResidual>(a, s);
-    if (epi == kSwiGLU) return launch_gemv<T, F, kSwiGLU>(a, s);
-    return launch_gemv<T, F, kPlain>(a, s);
+    a.m[0] = g.m0;
+    a.m[1] = g.m1;
+    a.m[2] = g.m2;
+    a.rows[0] = g.r0;
+    a.rows[1] = g.r1;
+    a.rows[2] = g.r2;
+    a.in = g.in;
+    a.out = g.out;
+    a.x = g.x;
+    a.norm_w = g.norm_w;
+    a.eps = g.eps;
+    a.res = g.res;
+    a.y = g.y;
+    a.part_v = g.part_v;
+    a.part_i = g.part_i;
+    a.ticket = g.ticket;
+    a.tokens = g.tokens;
+    a.next_token = g.next_token;
+    a.step = g.step;
+    a.position = g.position;
+    switch (g.epi) {
+        case kResidual: return launch_gemv<T, F, kResidual>(a, s);
+        case kSwiGLU: return launch_gemv<T, F, kSwiGLU>(a, s);
+        case kArgmax: return launch_gemv<T, F, kArgmax>(a, s);
+        default: return launch_gemv<T, F, kPlain>(a, s);
+    }
 }
 
 template <typename T>
-bool gemv_fmt(WF f, const void *m0, int r0, const void *m1, int r1, const void *m2, int r2,
-              int in, int out, const void *x, const void *res, void *y, int epi,
-              cudaStream_t s) {
-    if (f == WF::Q8) return gemv<T, WF::Q8>(m0, r0, m1, r1, m2, r2, in, out, x, res, y, epi, s);
-    if (f == WF::Q4) return gemv<T, WF::Q4>(m0, r0, m1, r1, m2, r2, in, out, x, res, y, epi, s);
-    return gemv<T, WF::Dense>(m0, r0, m1, r1, m2, r2, in, out, x, res, y, epi, s);
+bool run_gemv(WF f, const Gemv &g, cudaStream_t s) {
+    if (f == WF::Q8) return run_gemv_f<T, WF::Q8>(g, s);
+    if (f == WF::Q4) return run_gemv_f<T, WF::Q4>(g, s);
+    return run_gemv_f<T, WF::Dense>(g, s);
 }
 
 // Bytes of an [out][in] matrix in format f with element type T.
@@ -594,13 +688,16 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
     // ---- scratch ----
     const size_t qkvw = D.hidden + 2 * D.kvw;
     const size_t sizes[8] = {D.hidden, D.hidden, qkvw, D.hidden, D.hidden, D.hidden, D.hidden,
-                             D.inter};  // x n qkv qrot attn r n2 act
+                             D.inter};  // x (spare) qkv qrot attn r (spare) act
     size_t blk_bytes = 0;
     for (size_t z : sizes) blk_bytes += (z * es + 255) & ~size_t(255);
+    // tokens: [count] outputs, current token, visible length, argmax ticket,
+    // then the argmax partials of the lm_head CTAs
+    const size_t head_words = (D.count + 5 + 63) & ~size_t(63);
     if (!grow(&c.blk, &c.cap_blk, blk_bytes) ||
         !grow(&c.logits, &c.cap_logits, D.vocab * es) ||
         !grow(reinterpret_cast<void **>(&c.tokens), &c.cap_tokens,
-              (D.count + 2) * sizeof(uint32_t)))
+              (head_words + 2 * kGemvMaxGrid) * sizeof(uint32_t)))
         return false;
     void *buf[8];
     {
@@ -610,10 +707,20 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
             p += (sizes[i] * es + 255) & ~size_t(255);
         }
     }
-    void *x = buf[0], *n = buf[1], *qkv = buf[2], *qrot = buf[3], *attn = buf[4], *r = buf[5],
-         *n2 = buf[6], *act = buf[7];
+    void *x = buf[0], *qkv = buf[2], *qrot = buf[3], *attn = buf[4], *r = buf[5], *act = buf[7];
     uint32_t *cur = c.tokens + D.count;
     int32_t *seq_len = reinterpret_cast<int32_t *>(c.tokens + D.count + 1);
+    unsigned *ticket = c.tokens + D.count + 2;
+    int32_t *step = reinterpret_cast<int32_t *>(c.tokens + D.count + 3);
+    int32_t *position = reinterpret_cast<int32_t *>(c.tokens + D.count + 4);
+    float *part_v = reinterpret_cast<float *>(c.tokens + head_words);
+    int *part_i = reinterpret_cast<int *>(c.tokens + head_words + kGemvMaxGrid);
+    {
+        const int32_t init[3] = {0, 0, (int32_t)D.past};  // ticket, step, position
+        if (cudaMemcpyAsync(ticket, init, sizeof(init), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return false;
+    }
 
     // ---- layer pools and prefix import ----
     std::vector<PkvPagedLayer> pl(D.layers);
@@ -660,18 +767,18 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
 
     const float scale = 1.0f / sqrtf((float)D.hd);
     const int hidden = (int)D.hidden, kvw = (int)D.kvw, inter = (int)D.inter;
-    for (size_t t = 0; t < D.count; ++t) {
-        const int position = (int)(D.past + t);
+    // one token: the same launches every step (position and output slot are
+    // device-side), so they are captured once and replayed as a CUDA graph
+    auto enqueue_token = [&]() -> bool {
         embed_kernel<T><<<(hidden + 255) / 256, 256, 0, s>>>(
             static_cast<const T *>(emb), cur, static_cast<T *>(x), hidden, (uint32_t)D.vocab);
         for (size_t l = 0; l < D.layers; ++l) {
             const DevLayer &w = L[l];
-            rms_kernel<T><<<1, 1024, 0, s>>>(static_cast<const T *>(x),
-                                             static_cast<const T *>(w.input_norm),
-                                             static_cast<T *>(n), hidden, D.eps);
-            if (!gemv_fmt<T>(fmt, w.q, hidden, w.k, kvw, w.v, kvw, hidden, (int)qkvw, n,
-                             nullptr, qkv, kPlain, s))
-                return false;
+            Gemv g;  // qkv = [Wq; Wk; Wv] . rms(x)
+            g.m0 = w.q; g.r0 = hidden; g.m1 = w.k; g.r1 = kvw; g.m2 = w.v; g.r2 = kvw;
+            g.in = hidden; g.out = (int)qkvw; g.x = x; g.norm_w = w.input_norm; g.eps = D.eps;
+            g.y = qkv;
+            if (!run_gemv<T>(fmt, g, s)) return false;
             const int width = hidden > kvw ? hidden : kvw;
             rope_store_kernel<T><<<(width + 255) / 256, 256, 0, s>>>(
                 static_cast<const T *>(qkv), static_cast<T *>(qrot),
@@ -684,9 +791,9 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
                 PkvBatch one = batch;
                 one.seq_lens = seq_len;
                 one.batch = 1;
-                done = pkv_paged_decode(&pl[l], &one, D.qh, qrot, scale, attn,
-                                        PKV_DTYPE_F16, D.target, 0, c.ws, c.cap_ws,
-                                        (PkvStream)s, nullptr, 0) != 0;
+                done = pkv_paged_decode(&pl[l], &one, D.qh, qrot, scale, attn, PKV_DTYPE_F16,
+                                        D.target, 0, c.ws, c.cap_ws, (PkvStream)s, nullptr,
+                                        0) != 0;
             }
             if (!done) {
                 attn_split_kernel<T><<<dim3((unsigned)D.qh, (unsigned)splits), kAttnThreads, 0, s>>>(
@@ -697,25 +804,53 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
                 attn_merge_kernel<T><<<(unsigned)D.qh, 128, 0, s>>>(c.apart, splits, (int)D.hd,
                                                                     static_cast<T *>(attn));
             }
-            if (!gemv_fmt<T>(fmt, w.o, hidden, nullptr, 0, nullptr, 0, hidden, hidden, attn, x,
-                             r, kResidual, s))
-                return false;
-            rms_kernel<T><<<1, 1024, 0, s>>>(static_cast<const T *>(r),
-                                             static_cast<const T *>(w.post_norm),
-                                             static_cast<T *>(n2), hidden, D.eps);
-            if (!gemv_fmt<T>(fmt, w.gate, inter, w.up, inter, nullptr, 0, hidden, inter, n2,
-                             nullptr, act, kSwiGLU, s) ||
-                !gemv_fmt<T>(fmt, w.down, hidden, nullptr, 0, nullptr, 0, inter, hidden, act,
-                             r, x, kResidual, s))
+            Gemv o;  // r = Wo . attn + x
+            o.m0 = w.o; o.r0 = hidden; o.in = hidden; o.out = hidden; o.x = attn; o.res = x;
+            o.y = r; o.epi = kResidual;
+            Gemv gu;  // act = silu(Wg . rms(r)) * (Wu . rms(r))
+            gu.m0 = w.gate; gu.r0 = inter; gu.m1 = w.up; gu.r1 = inter; gu.in = hidden;
+            gu.out = inter; gu.x = r; gu.norm_w = w.post_norm; gu.eps = D.eps; gu.y = act;
+            gu.epi = kSwiGLU;
+            Gemv dn;  // x = Wd . act + r
+            dn.m0 = w.down; dn.r0 = hidden; dn.in = inter; dn.out = hidden; dn.x = act;
+            dn.res = r; dn.y = x; dn.epi = kResidual;
+            if (!run_gemv<T>(fmt, o, s) || !run_gemv<T>(fmt, gu, s) || !run_gemv<T>(fmt, dn, s))
                 return false;
         }
-        rms_kernel<T><<<1, 1024, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(fnorm),
-                                         static_cast<T *>(n), hidden, D.eps);
-        if (!gemv_fmt<T>(fmt, head, (int)D.vocab, nullptr, 0, nullptr, 0, hidden, (int)D.vocab,
-                         n, nullptr, c.logits, kPlain, s))
+        Gemv hd;  // logits = lm_head . rms(x) * final_norm, then the first argmax
+        hd.m0 = head; hd.r0 = (int)D.vocab; hd.in = hidden; hd.out = (int)D.vocab; hd.x = x;
+        hd.norm_w = fnorm; hd.eps = D.eps; hd.y = c.logits; hd.epi = kArgmax;
+        hd.part_v = part_v; hd.part_i = part_i; hd.ticket = ticket; hd.tokens = c.tokens;
+        hd.next_token = cur; hd.step = step; hd.position = position;
+        return run_gemv<T>(fmt, hd, s);
+    };
+    bool graphed = false;
+    if (D.count > 1) {
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const bool enq = enqueue_token();
+            const cudaError_t end = cudaStreamEndCapture(s, &graph);
+            if (enq && end == cudaSuccess && graph != nullptr &&
+                cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+                graphed = true;
+                for (size_t t = 0; graphed && t < D.count; ++t)
+                    graphed = cudaGraphLaunch(exec, s) == cudaSuccess;
+            }
+        }
+        if (exec != nullptr) cudaGraphExecDestroy(exec);
+        if (graph != nullptr) cudaGraphDestroy(graph);
+        cudaGetLastError();  // a failed capture falls back to direct launches
+        if (!graphed && cudaStreamSynchronize(s) != cudaSuccess) return false;
+    }
+    if (!graphed) {
+        // direct launches; after a failed replay the step counter tells where to resume
+        int32_t done = 0;
+        if (D.count > 1 &&
+            cudaMemcpy(&done, step, sizeof(done), cudaMemcpyDeviceToHost) != cudaSuccess)
             return false;
-        argmax_kernel<T><<<1, kArgmaxThreads, 0, s>>>(static_cast<const T *>(c.logits),
-                                                      (int)D.vocab, c.tokens + t, cur);
+        for (size_t t = (size_t)done; t < D.count; ++t)
+            if (!enqueue_token()) return false;
     }
     if (cudaGetLastError() != cudaSuccess) return false;
     if (cudaMemcpyAsync(rq->generated_tokens, c.tokens, D.count * sizeof(uint32_t),
@@ -753,6 +888,8 @@ bool valid_dims(const TensorPagedKVDecodeRequest *r, size_t capacity, bool quant
     const size_t kvw = kvh * hd;
     if (kvw > (size_t)INT32_MAX / 4 || capacity > SIZE_MAX / kvw) return false;
     if (quantized && (h % 32 || r->intermediate_size % 32 || kvw % 32)) return false;
+    // GEMV inputs are staged in shared memory
+    if (h > (size_t)kGemvMaxIn || r->intermediate_size > (size_t)kGemvMaxIn) return false;
     return true;
 }
 
