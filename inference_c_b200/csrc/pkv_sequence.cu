@@ -197,6 +197,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     __shared__ int redi[kGemvThreads / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int warps = kGemvThreads / 32;
+    pdl_launch_dependents();
+    // The weights do not depend on earlier kernels: start pulling the first
+    // 2 KiB of this warp's first row into L2 while they finish.
+    {
+        const int r = blockIdx.x * warps + warp;
+        if (F == WF::Dense && r < a.out && r < a.rows[0]) {
+            const char *w = static_cast<const char *>(a.m[0]) + (size_t)r * a.in * sizeof(T);
+            const int bytes = min(a.in * (int)sizeof(T), 2048);
+            if (lane * 128 < bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(w + lane * 128));
+        }
+    }
+    pdl_wait();  // x, the residual and the argmax ticket come from earlier kernels
     const T *x = static_cast<const T *>(a.x);
     if (NORM) {
         // RMSNorm (attention_cuda.cu:106-124): x * rsqrt(mean(x^2) + eps) * w
@@ -299,6 +311,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 template <typename T>
 __global__ void embed_kernel(const T *emb, const uint32_t *token, T *x, int width,
                              uint32_t vocab) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t t = *token;
     if (t >= vocab) {
         if (blockIdx.x == 0 && threadIdx.x == 0) record_fault(&g_sequence_fault, kFaultPositionOutOfRange);
@@ -317,6 +331,8 @@ __global__ void rope_store_kernel(const T *qkv, T *qrot, T *kpool, T *vpool,
                                   const uint32_t *table, int table_stride, int block_size,
                                   uint32_t block_count, int hidden, int kv_width, int head_dim,
                                   const int32_t *position_dev, float theta, int32_t *seq_len) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int index = blockIdx.x * blockDim.x + threadIdx.x;
     const int half_dim = head_dim / 2;
     const int position = *position_dev;
@@ -382,6 +398,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
     __shared__ float wo[8][256];
     const int h = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
     const int L = *seq_len;
     const int kvh = h / (q_heads / kv_heads);
     const int kv_width = kv_heads * head_dim;
@@ -452,6 +470,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(
 
 template <typename T>
 __global__ void attn_merge_kernel(const float *part, int splits, int head_dim, T *out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x;
     const float *p = part + (size_t)h * splits * (head_dim + 2);
     float M = -INFINITY;
@@ -550,6 +570,25 @@ struct Dims {
     float eps, theta;
 };
 
+// Launches with programmatic dependent launch: the kernel may start while the
+// one before it in the stream finishes; every decoder kernel waits
+// (griddepcontrol.wait) before it reads what earlier kernels wrote.
+template <typename... KArgs, typename... Args>
+bool launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess;
+}
+
 template <typename T, WF F, int EPI, bool NORM>
 bool launch_gemv_n(const GemvArgs &a, cudaStream_t s) {
     const int warps = kGemvThreads / 32;
@@ -566,8 +605,7 @@ bool launch_gemv_n(const GemvArgs &a, cudaStream_t s) {
             return false;
         configured[dev] = true;
     }
-    gemv_kernel<T, F, EPI, NORM><<<grid, kGemvThreads, smem, s>>>(a);
-    return cudaGetLastError() == cudaSuccess;
+    return launch_pdl(gemv_kernel<T, F, EPI, NORM>, dim3(grid), dim3(kGemvThreads), smem, s, a);
 }
 
 template <typename T, WF F, int EPI>
@@ -770,8 +808,10 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
     // one token: the same launches every step (position and output slot are
     // device-side), so they are captured once and replayed as a CUDA graph
     auto enqueue_token = [&]() -> bool {
-        embed_kernel<T><<<(hidden + 255) / 256, 256, 0, s>>>(
-            static_cast<const T *>(emb), cur, static_cast<T *>(x), hidden, (uint32_t)D.vocab);
+        if (!launch_pdl(embed_kernel<T>, dim3((hidden + 255) / 256), dim3(256), 0, s,
+                        static_cast<const T *>(emb), (const uint32_t *)cur, static_cast<T *>(x),
+                        hidden, (uint32_t)D.vocab))
+            return false;
         for (size_t l = 0; l < D.layers; ++l) {
             const DevLayer &w = L[l];
             Gemv g;  // qkv = [Wq; Wk; Wv] . rms(x)
@@ -780,12 +820,13 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
             g.y = qkv;
             if (!run_gemv<T>(fmt, g, s)) return false;
             const int width = hidden > kvw ? hidden : kvw;
-            rope_store_kernel<T><<<(width + 255) / 256, 256, 0, s>>>(
-                static_cast<const T *>(qkv), static_cast<T *>(qrot),
-                static_cast<T *>(pl[l].key_pool), static_cast<T *>(pl[l].value_pool),
-                batch.block_tables, (int)batch.table_stride, (int)pl[l].block_size,
-                (uint32_t)pl[l].block_count, hidden, kvw, (int)D.hd, position, D.theta,
-                seq_len);
+            if (!launch_pdl(rope_store_kernel<T>, dim3((width + 255) / 256), dim3(256), 0, s,
+                            static_cast<const T *>(qkv), static_cast<T *>(qrot),
+                            static_cast<T *>(pl[l].key_pool), static_cast<T *>(pl[l].value_pool),
+                            batch.block_tables, (int)batch.table_stride, (int)pl[l].block_size,
+                            (uint32_t)pl[l].block_count, hidden, kvw, (int)D.hd,
+                            (const int32_t *)position, D.theta, seq_len))
+                return false;
             bool done = false;
             if (fast) {
                 PkvBatch one = batch;
@@ -796,13 +837,17 @@ bool run_decoder(const TensorPagedKVDecodeRequest *rq, const Dims &D, WF fmt, Pk
                                         0) != 0;
             }
             if (!done) {
-                attn_split_kernel<T><<<dim3((unsigned)D.qh, (unsigned)splits), kAttnThreads, 0, s>>>(
-                    static_cast<const T *>(qrot), static_cast<const T *>(pl[l].key_pool),
-                    static_cast<const T *>(pl[l].value_pool), batch.block_tables,
-                    (int)batch.table_stride, (int)pl[l].block_size, (uint32_t)pl[l].block_count,
-                    seq_len, (int)D.qh, (int)D.kvh, (int)D.hd, scale, c.apart);
-                attn_merge_kernel<T><<<(unsigned)D.qh, 128, 0, s>>>(c.apart, splits, (int)D.hd,
-                                                                    static_cast<T *>(attn));
+                if (!launch_pdl(attn_split_kernel<T>, dim3((unsigned)D.qh, (unsigned)splits),
+                                dim3(kAttnThreads), 0, s, static_cast<const T *>(qrot),
+                                static_cast<const T *>(pl[l].key_pool),
+                                static_cast<const T *>(pl[l].value_pool), batch.block_tables,
+                                (int)batch.table_stride, (int)pl[l].block_size,
+                                (uint32_t)pl[l].block_count, (const int32_t *)seq_len, (int)D.qh,
+                                (int)D.kvh, (int)D.hd, scale, c.apart) ||
+                    !launch_pdl(attn_merge_kernel<T>, dim3((unsigned)D.qh), dim3(128), 0, s,
+                                (const float *)c.apart, splits, (int)D.hd,
+                                static_cast<T *>(attn)))
+                    return false;
             }
             Gemv o;  // r = Wo . attn + x
             o.m0 = w.o; o.r0 = hidden; o.in = hidden; o.out = hidden; o.x = attn; o.res = x;
