@@ -142,6 +142,12 @@ EXPORTS = {
     "pkv_paged_prefill": (_c_int, [_LP, _BP, _c_size, _c_ptr, _c_ptr, _c_size, _c_size,
                                    ctypes.c_float, _c_int, _c_ptr, _c_int, _c_ptr, *_ERR]),
     "pkv_device_fault": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_uint32), *_ERR]),
+    "pkv_sdpa_workspace_bytes": (_c_size, [_c_size, _c_size, _c_size, _c_size, _c_size]),
+    "pkv_sdpa_f16": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size, _c_size, _c_size,
+                              _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_sdpa_f16_host": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size,
+                                   _c_size, _c_size, _c_size, _c_size, _c_size, ctypes.c_float,
+                                   _c_int]),
     # include/pkv_b200.h -- host transaction layer
     "pkv_pool_create": (_c_int, [_c_ptr, _c_int, _c_int, _c_size, _c_size, _c_size, _c_size,
                                  _c_size, ctypes.POINTER(_c_ptr), *_ERR]),
@@ -483,3 +489,34 @@ def decode_sequence_paged(cache: "PagedKVCache", sequence: int, storage: int, la
 
 def decode_cache_clear() -> None:
     load().tensor_attention_decode_cache_clear()
+
+
+# ---------------------------------------------------------------------------
+# Dense FP16 SDPA (tensor_sdpa_f16's backend) on the prefill kernel
+# ---------------------------------------------------------------------------
+
+def sdpa_f16(query, key, value, output, scale: float, causal: bool, stream=None) -> None:
+    """query/output [B, Hq, Lq, 128], key/value [B, Hkv, Lk, 128] float16 CUDA tensors."""
+    import torch
+    B, Hq, Lq, d = query.shape
+    Hkv, Lk = key.shape[1], key.shape[2]
+    n = load().pkv_sdpa_workspace_bytes(B, Hq, Hkv, Lq, Lk)
+    ws = torch.empty(n, dtype=torch.uint8, device=query.device)
+    _call("pkv_sdpa_f16", query.data_ptr(), key.data_ptr(), value.data_ptr(), output.data_ptr(),
+          B, Hq, Hkv, Lq, Lk, ctypes.c_float(scale), int(causal), ws.data_ptr(), n,
+          _stream_ptr(stream))
+
+
+def sdpa_f16_host(query, key, value, scale: float, causal: bool, mask=None):
+    """The run_f16 backend hook with host numpy uint16 (FP16 bits) arrays;
+    returns the output bits or None when the call returns 0."""
+    import numpy as np
+    B, Hq, Lq, d = query.shape
+    Hkv, Lk, dv = key.shape[1], key.shape[2], value.shape[3]
+    q, k, v = (np.ascontiguousarray(a, dtype=np.uint16) for a in (query, key, value))
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint16)
+    out = np.zeros((B, Hq, Lq, dv), dtype=np.uint16)
+    ok = load().pkv_sdpa_f16_host(q.ctypes.data, k.ctypes.data, v.ctypes.data,
+                                  None if m is None else m.ctypes.data, out.ctypes.data, B, Hq,
+                                  Hkv, Lq, Lk, d, dv, ctypes.c_float(scale), int(causal))
+    return out if ok else None

@@ -22,7 +22,7 @@ LIBDIR = HERE / "lib"
 LIBRARY = LIBDIR / "libpkv_b200.so"
 
 C_SOURCES = ["paged_kv_cache.c", "pkv_pool.c"]
-CU_SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_sequence.cu"]
+CU_SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_sequence.cu", "pkv_dense.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

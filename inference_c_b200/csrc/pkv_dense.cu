@@ -1,0 +1,246 @@
+// pkv_dense.cu -- dense FP16 SDPA served by the tcgen05 paged prefill kernel.
+//
+// The SDK's tensor_sdpa_f16 (src/common/attention.c:408-459) hands its
+// backend [batch][heads][length][dim] FP16 tensors (run_f16 of
+// src/attention_backend.h; the CUDA backend's sdpa<T>, attention_cuda.cu:
+// 25-99, materialises every score row).  Here each (batch, KV head) becomes
+// one "sequence" of the paged prefill kernel with an identity page table:
+//   * K and V of (b, g) are kv_len contiguous rows of 128 elements, i.e. a
+//     pool with one KV head whose pages are consecutive; when kv_len is a
+//     multiple of 16 the tensors themselves are the pool (no copy), otherwise
+//     each sequence is copied to a whole number of 16-row pages;
+//   * the group's query heads go to a token-major [rows][G][128] buffer and
+//     the output comes back the same way (two transpose kernels);
+//   * the causal rule key > query + (kv_len - q_len) is the prefill kernel's
+//     own, so q_len <= kv_len is required.
+// head_dim = value_dim = 128; additive masks are not taken (the call fails).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "pkv_b200.h"
+#include "pkv_internal.h"
+
+namespace pkv {
+namespace {
+
+constexpr int kDHead = 128;
+constexpr int kPage = 16;
+constexpr int kChunks = kDHead / 8;  // 16-byte chunks per row
+
+// Q [B][Hq][Lq][128] -> Q' [(b*Hkv + g)*Lq + i][j][128], h = g*G + j (and back).
+__global__ void regroup_kernel(const uint4 *src, uint4 *dst, int64_t B, int Hq, int G, int Lq,
+                               bool to_rows) {
+    const int64_t n = B * Hq * (int64_t)Lq * kChunks;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(e % kChunks);
+        int64_t r = e / kChunks;
+        const int i = (int)(r % Lq);
+        r /= Lq;
+        const int h = (int)(r % Hq);
+        const int64_t b = r / Hq;
+        const int g = h / G, j = h - g * G;
+        const int64_t dense = ((b * Hq + h) * Lq + i) * kChunks + c;
+        const int64_t rows = (((b * (Hq / G) + g) * Lq + i) * G + j) * kChunks + c;
+        if (to_rows) dst[rows] = src[dense];
+        else dst[dense] = src[rows];
+    }
+}
+
+// K or V of every (b, g) into a whole number of 16-row pages.
+__global__ void pad_rows_kernel(const uint4 *src, uint4 *dst, int64_t S, int Lk, int pages) {
+    const int64_t n = S * (int64_t)Lk * kChunks;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(e % kChunks);
+        const int64_t r = e / kChunks;
+        const int64_t s = r / Lk;
+        const int i = (int)(r - s * Lk);
+        dst[((s * pages * kPage) + i) * kChunks + c] = src[e];
+    }
+}
+
+// Identity page tables, lengths and query row offsets of the S sequences.
+__global__ void tables_kernel(uint32_t *tables, int32_t *lens, int32_t *offs, int64_t S,
+                              int pages, int Lk, int Lq) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < S * pages;
+         e += (int64_t)gridDim.x * blockDim.x)
+        tables[e] = (uint32_t)e;  // sequence s, page p -> pool page s * pages + p
+    for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s <= S;
+         s += (int64_t)gridDim.x * blockDim.x) {
+        if (s < S) lens[s] = Lk;
+        offs[s] = (int32_t)(s * Lq);
+    }
+}
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+struct DenseLayout {
+    size_t qrows, orows, tables, lens, offs, kpad, vpad, total;
+};
+
+DenseLayout dense_layout(size_t B, size_t Hq, size_t Hkv, size_t Lq, size_t Lk) {
+    const size_t S = B * Hkv, pages = (Lk + kPage - 1) / kPage;
+    const bool pad = Lk % kPage != 0;
+    DenseLayout w;
+    w.qrows = 0;
+    w.orows = align256(B * Hq * Lq * kDHead * 2);
+    w.tables = w.orows + align256(B * Hq * Lq * kDHead * 2);
+    w.lens = w.tables + align256(S * pages * 4);
+    w.offs = w.lens + align256(S * 4);
+    w.kpad = w.offs + align256((S + 1) * 4);
+    w.vpad = w.kpad + (pad ? align256(S * pages * kPage * kDHead * 2) : 0);
+    w.total = w.vpad + (pad ? align256(S * pages * kPage * kDHead * 2) : 0);
+    return w;
+}
+
+int grid_for(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    return (int)(g < 148 * 16 ? (g < 1 ? 1 : g) : 148 * 16);
+}
+
+std::mutex g_host_mutex;
+void *g_host_ws[64];
+size_t g_host_ws_bytes[64];
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" {
+
+size_t pkv_sdpa_workspace_bytes(size_t batch, size_t q_heads, size_t kv_heads, size_t q_len,
+                                size_t kv_len) {
+    return pkv::dense_layout(batch, q_heads, kv_heads, q_len, kv_len).total;
+}
+
+int pkv_sdpa_f16(const void *query, const void *key, const void *value, void *output,
+                 size_t batch, size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
+                 float scale, int causal, void *workspace, size_t workspace_bytes,
+                 PkvStream stream, char *error, size_t error_capacity) {
+    using namespace pkv;
+    const char *what = "pkv_sdpa_f16";
+    if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
+        workspace == nullptr) {
+        pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    if (batch == 0 || q_heads == 0 || kv_heads == 0 || q_len == 0 || kv_len == 0 ||
+        q_heads % kv_heads != 0 || q_heads / kv_heads > 65535 || q_len > kv_len ||
+        kv_len > (1u << 30) || batch * kv_heads > (1u << 24) ||
+        batch * q_heads * q_len >= (size_t(1) << 31) || (causal != 0 && causal != 1)) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: needs q_heads a multiple of kv_heads and q_len <= kv_len",
+                               what);
+        return 0;
+    }
+    const DenseLayout w = dense_layout(batch, q_heads, kv_heads, q_len, kv_len);
+    if (workspace_bytes < w.total || (uintptr_t)workspace % 256 ||
+        ((uintptr_t)query | (uintptr_t)key | (uintptr_t)value | (uintptr_t)output) % 16) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: workspace needs %zu bytes (256-aligned), tensors 16-aligned",
+                               what, w.total);
+        return 0;
+    }
+    const cudaStream_t s = (cudaStream_t)stream;
+    auto *ws = static_cast<unsigned char *>(workspace);
+    const int64_t S = (int64_t)(batch * kv_heads);
+    const int G = (int)(q_heads / kv_heads);
+    const int pages = (int)((kv_len + kPage - 1) / kPage);
+    const bool pad = kv_len % kPage != 0;
+    auto *qrows = reinterpret_cast<uint4 *>(ws + w.qrows);
+    auto *orows = reinterpret_cast<uint4 *>(ws + w.orows);
+    auto *tables = reinterpret_cast<uint32_t *>(ws + w.tables);
+    auto *lens = reinterpret_cast<int32_t *>(ws + w.lens);
+    auto *offs = reinterpret_cast<int32_t *>(ws + w.offs);
+    const void *kpool = key, *vpool = value;
+    const int64_t qn = (int64_t)(batch * q_heads * q_len) * kChunks;
+    regroup_kernel<<<grid_for(qn), 256, 0, s>>>(static_cast<const uint4 *>(query), qrows,
+                                                 (int64_t)batch, (int)q_heads, G, (int)q_len,
+                                                 true);
+    tables_kernel<<<grid_for(S * pages + S + 1), 256, 0, s>>>(tables, lens, offs, S, pages,
+                                                              (int)kv_len, (int)q_len);
+    if (pad) {
+        const int64_t kn = S * (int64_t)kv_len * kChunks;
+        pad_rows_kernel<<<grid_for(kn), 256, 0, s>>>(static_cast<const uint4 *>(key),
+                                                      reinterpret_cast<uint4 *>(ws + w.kpad), S,
+                                                      (int)kv_len, pages);
+        pad_rows_kernel<<<grid_for(kn), 256, 0, s>>>(static_cast<const uint4 *>(value),
+                                                      reinterpret_cast<uint4 *>(ws + w.vpad), S,
+                                                      (int)kv_len, pages);
+        kpool = ws + w.kpad;
+        vpool = ws + w.vpad;
+    }
+    if (cudaGetLastError() != cudaSuccess) {
+        pkv_internal_set_error(error, error_capacity, "%s: launch failed", what);
+        return 0;
+    }
+    PkvPagedLayer layer;
+    layer.key_pool = const_cast<void *>(kpool);
+    layer.value_pool = const_cast<void *>(vpool);
+    layer.block_size = kPage;
+    layer.block_count = (size_t)S * pages;
+    layer.kv_heads = 1;
+    layer.head_dim = kDHead;
+    layer.dtype = PKV_DTYPE_F16;
+    PkvBatch b;
+    b.block_tables = tables;
+    b.table_stride = (size_t)pages;
+    b.seq_lens = lens;
+    b.batch = (size_t)S;
+    if (!pkv_paged_prefill(&layer, &b, (size_t)G, offs, qrows, (size_t)(S * (int64_t)q_len),
+                           q_len, scale, causal, orows, PKV_DTYPE_F16, stream, error,
+                           error_capacity))
+        return 0;
+    regroup_kernel<<<grid_for(qn), 256, 0, s>>>(orows, static_cast<uint4 *>(output),
+                                                 (int64_t)batch, (int)q_heads, G, (int)q_len,
+                                                 false);
+    if (cudaGetLastError() != cudaSuccess) {
+        pkv_internal_set_error(error, error_capacity, "%s: launch failed", what);
+        return 0;
+    }
+    return 1;
+}
+
+int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t *value,
+                      const uint16_t *additive_mask, uint16_t *output, size_t batch,
+                      size_t query_heads, size_t kv_heads, size_t query_length,
+                      size_t kv_length, size_t head_dim, size_t value_dim, float scale,
+                      int causal) {
+    using namespace pkv;
+    if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
+        additive_mask != nullptr || head_dim != kDHead || value_dim != kDHead ||
+        batch == 0 || query_heads == 0 || kv_heads == 0 || query_length == 0 ||
+        kv_length == 0 || query_heads % kv_heads != 0 || query_length > kv_length)
+        return 0;
+    std::lock_guard<std::mutex> lock(g_host_mutex);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    const size_t qb = batch * query_heads * query_length * kDHead * 2;
+    const size_t kb = batch * kv_heads * kv_length * kDHead * 2;
+    const size_t wsb = pkv_sdpa_workspace_bytes(batch, query_heads, kv_heads, query_length,
+                                                kv_length);
+    const size_t need = align256(qb) * 2 + align256(kb) * 2 + wsb;
+    if (g_host_ws_bytes[dev] < need) {
+        if (g_host_ws[dev] != nullptr) cudaFree(g_host_ws[dev]);
+        g_host_ws[dev] = nullptr;
+        g_host_ws_bytes[dev] = 0;
+        if (cudaMalloc(&g_host_ws[dev], need) != cudaSuccess) return 0;
+        g_host_ws_bytes[dev] = need;
+    }
+    auto *base = static_cast<unsigned char *>(g_host_ws[dev]);
+    unsigned char *dq = base, *dout = dq + align256(qb), *dk = dout + align256(qb);
+    unsigned char *dv = dk + align256(kb), *dws = dv + align256(kb);
+    // the SDK's backends are synchronous and use the default stream
+    if (cudaMemcpy(dq, query, qb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dk, key, kb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dv, value, kb, cudaMemcpyHostToDevice) != cudaSuccess)
+        return 0;
+    if (!pkv_sdpa_f16(dq, dk, dv, dout, batch, query_heads, kv_heads, query_length, kv_length,
+                      scale, causal, dws, wsb, nullptr, nullptr, 0))
+        return 0;
+    return cudaMemcpy(output, dout, qb, cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+}  // extern "C"
