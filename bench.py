@@ -53,7 +53,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=3)
+    p.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6, 7], default=3)
     p.add_argument("--chunk", type=int, default=0, help="decode split size in tokens (0: auto)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -995,6 +995,104 @@ def run_decoder(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Config 7: dense FP16 SDPA (tensor_sdpa_f16's backend) on the prefill kernel
+# ---------------------------------------------------------------------------
+
+CFG7 = dict(batch=1, q_heads=32, kv_heads=8, q_len=4096, kv_len=4096, head_dim=128, causal=True)
+
+
+def cfg7_flops() -> float:
+    c = CFG7
+    off = c["kv_len"] - c["q_len"]
+    keys = sum(min(c["kv_len"], off + i + 1) for i in range(c["q_len"]))
+    return 4.0 * c["head_dim"] * c["batch"] * c["q_heads"] * keys
+
+
+def run_dense(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    c = CFG7
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    B, Hq, Hkv, Lq, Lk = c["batch"], c["q_heads"], c["kv_heads"], c["q_len"], c["kv_len"]
+    q = torch.randn(B, Hq, Lq, 128, generator=g, device=dev).half()
+    k = torch.randn(B, Hkv, Lk, 128, generator=g, device=dev).half()
+    v = torch.randn(B, Hkv, Lk, 128, generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    scale = 1 / math.sqrt(128)
+    flops = cfg7_flops()
+    peak, kind = measured_peak_tflops()
+    steps, warmup = args.steps, args.warmup
+    block = {"workload": "cfg7: dense causal FP16 SDPA, B=1, GQA 32/8, 4096 x 4096, d=128 "
+                         "(tensor_sdpa_f16's backend)", **c}
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
+    h_q, h_k, h_v = (t.cpu().numpy().view(np.uint16) for t in (q, k, v))
+    if args.impl == "reference":
+        from oracle import oracle as O
+        if not O.ref_cuda_available():
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "oracle/_ref/libref_cuda.so (the SDK's CUDA backend) not built"}))
+            return
+        run = O.ref_cuda_sdpa_f16
+        call = lambda: run(h_q, h_k, h_v, scale, True)
+    else:
+        import inference_c_b200 as P
+        P.load()
+        call = lambda: P.sdpa_f16_host(h_q, h_k, h_v, scale, True)
+    # e2e: the backend hook with host tensors (upload, attention, download)
+    with sampler:
+        for _ in range(warmup):
+            assert call() is not None
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            call()
+        e2e_ms = (time.perf_counter() - t0) / steps * 1e3
+        dev_ms = None
+        if args.impl != "reference":
+            s = torch.cuda.current_stream()
+            for _ in range(warmup):
+                P.sdpa_f16(q, k, v, out, scale, True)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(steps):
+                P.sdpa_f16(q, k, v, out, scale, True)
+            e1.record(s)
+            torch.cuda.synchronize()
+            dev_ms = e0.elapsed_time(e1) / steps
+    ms = dev_ms if dev_ms is not None else e2e_ms
+    value = flops / (ms / 1e3) / 1e12
+    bytes_h = (q.numel() + k.numel() + v.numel()) * 2
+    line = {
+        "metric": "dense causal SDPA TFLOP/s (config 7: tensor_sdpa_f16's backend)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic: seeded N(0,1) FP16", "config": block,
+        "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s",
+                     "frac": value / peak, "traffic": None, "peak_kind": kind,
+                     "algorithmic_flops_per_call": flops,
+                     "note": "device entry with resident tensors; includes the two regroup "
+                             "copies around the prefill kernel"},
+        "e2e": {"value": flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": bytes_h, "d2h_bytes_per_step": q.numel() * 2,
+                "api": "run_f16 backend hook with host tensors (pkv_sdpa_f16_host)"},
+        "gpu_launches": 4 * steps,
+        "clocks": sampler.summary(),
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+        line["gpu_launches"] = None
+        line["cpu_baseline"] = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                                "sample": "the SDK's own CUDA backend dense sdpa (run_f16, "
+                                          "attention_cuda.cu:71-99) on the same GPU"}
+        line["roofline"] = None
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill_reference(args) -> None:
     """--impl reference for config 5: the SDK's tensor_sdpa_f32 on a bounded
     slice of the workload each step."""
@@ -1023,7 +1121,9 @@ def run_prefill_reference(args) -> None:
 
 def main():
     args = parse_args()
-    if args.config == 6:
+    if args.config == 7:
+        run_dense(args)
+    elif args.config == 6:
         run_decoder(args)
     elif args.config == 5:
         run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)

@@ -378,3 +378,28 @@ class RefCudaDecoder:
             self.lib.tensor_paged_kv_cache_free(self.cache)
             self.lib.tensor_attention_decode_cache_clear()
             self.cache = None
+
+
+class _Ops(ctypes.Structure):
+    """The head of TensorAttentionBackendOps (the SDK's src/attention_backend.h)."""
+    _fields_ = [("kind", _i), ("name", ctypes.c_char_p), ("is_available", _p), ("run", _p),
+                ("run_f16", _p)]
+
+
+_RUN_F16 = ctypes.CFUNCTYPE(_i, _p, _p, _p, _p, _p, _s, _s, _s, _s, _s, _s, _s, _f, _i)
+
+
+def ref_cuda_sdpa_f16(q, k, v, scale: float, causal: bool):
+    """The SDK CUDA backend's run_f16 (dense sdpa, attention_cuda.cu:71-99)
+    on host uint16 arrays; returns the output bits or None."""
+    lib = ctypes.CDLL(str(REF_CUDA_PATH))
+    lib.tensor_attention_cuda_backend.restype = ctypes.POINTER(_Ops)
+    ops = lib.tensor_attention_cuda_backend().contents
+    run = _RUN_F16(ops.run_f16)
+    B, Hq, Lq, d = q.shape
+    Hkv, Lk, dv = k.shape[1], k.shape[2], v.shape[3]
+    q, k, v = (np.ascontiguousarray(a, dtype=np.uint16) for a in (q, k, v))
+    out = np.zeros((B, Hq, Lq, dv), dtype=np.uint16)
+    ok = run(q.ctypes.data, k.ctypes.data, v.ctypes.data, None, out.ctypes.data, B, Hq, Hkv, Lq,
+             Lk, d, dv, scale, int(causal))
+    return out if ok else None

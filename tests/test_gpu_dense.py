@@ -56,6 +56,11 @@ def test_host_hook_and_sdk_cpu(lib, oracle_mod, cuda):
     assert got is not None
     got = got.view(np.float16).astype(np.float32)
     check_close(got, expected(q, k, v, scale, True, oracle_mod), "host hook vs oracle")
+    if O.ref_cuda_available():  # the SDK's own CUDA backend (run_f16) on the same GPU
+        ref = O.ref_cuda_sdpa_f16(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), scale,
+                                  True)
+        assert ref is not None
+        check_close(got, ref.view(np.float16).astype(np.float32), "host hook vs SDK CUDA sdpa")
     if O.ref_available():  # the SDK's own tensor_sdpa_f32
         want = O.ref_sdpa_f32(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
                               scale, True)
