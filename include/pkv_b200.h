@@ -171,23 +171,25 @@ int pkv_device_fault(int device, uint32_t *code, char *error,
 
 /* Dense FP16 SDPA on the tcgen05 prefill kernel: query [batch][q_heads]
  * [q_len][128], key/value [batch][kv_heads][kv_len][128], output like query,
- * all device pointers (16-byte aligned).  GQA (q_heads a multiple of
- * kv_heads), causal rule key > query + (kv_len - q_len) (needs q_len <=
- * kv_len), FP32 accumulation, FP16 output.  Replaces the CUDA backend's
- * dense sdpa<T> (attention_cuda.cu:25-99) behind tensor_sdpa_f16
- * (attention.c:408-459); additive masks are not taken.  Each (batch, KV
- * head) is one sequence of pkv_paged_prefill with an identity page table. */
+ * optional additive mask [q_len][kv_len] (NULL: none; shared by every batch
+ * and head), all device pointers (tensors 16-byte aligned, the mask 2-byte).
+ * GQA (q_heads a multiple of kv_heads), score = q.k * scale + mask, causal
+ * rule key > query + max(kv_len - q_len, 0), FP32 accumulation, FP16 output;
+ * a row whose maximum score is not finite (all keys -inf, or a +inf) is
+ * zero.  Replaces the CUDA backend's dense sdpa<T> (attention_cuda.cu:25-99)
+ * behind tensor_sdpa_f16 (attention.c:408-459).  Each (batch, KV head) is
+ * one sequence of the paged prefill kernel with an identity page table. */
 size_t pkv_sdpa_workspace_bytes(size_t batch, size_t q_heads, size_t kv_heads,
                                 size_t q_len, size_t kv_len);
 int pkv_sdpa_f16(const void *query, const void *key, const void *value,
-                 void *output, size_t batch, size_t q_heads, size_t kv_heads,
-                 size_t q_len, size_t kv_len, float scale, int causal,
-                 void *workspace, size_t workspace_bytes, PkvStream stream,
-                 char *error, size_t error_capacity);
+                 const void *additive_mask, void *output, size_t batch,
+                 size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
+                 float scale, int causal, void *workspace, size_t workspace_bytes,
+                 PkvStream stream, char *error, size_t error_capacity);
 /* The same with host tensors, in the argument order of the SDK backend hook
  * run_f16 (src/attention_backend.h:14-18), so it can be installed as that
  * hook: uploads, computes on the current device, downloads, synchronous.
- * Returns 0 for a mask, head_dim/value_dim other than 128, or q_len > kv_len. */
+ * Returns 0 for head_dim/value_dim other than 128. */
 int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key,
                       const uint16_t *value, const uint16_t *additive_mask,
                       uint16_t *output, size_t batch, size_t query_heads,

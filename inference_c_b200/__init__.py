@@ -143,8 +143,9 @@ EXPORTS = {
                                    ctypes.c_float, _c_int, _c_ptr, _c_int, _c_ptr, *_ERR]),
     "pkv_device_fault": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_uint32), *_ERR]),
     "pkv_sdpa_workspace_bytes": (_c_size, [_c_size, _c_size, _c_size, _c_size, _c_size]),
-    "pkv_sdpa_f16": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size, _c_size, _c_size,
-                              _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_sdpa_f16": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size, _c_size,
+                              _c_size, _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size, _c_ptr,
+                              *_ERR]),
     "pkv_sdpa_f16_host": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size,
                                    _c_size, _c_size, _c_size, _c_size, _c_size, ctypes.c_float,
                                    _c_int]),
@@ -495,16 +496,18 @@ def decode_cache_clear() -> None:
 # Dense FP16 SDPA (tensor_sdpa_f16's backend) on the prefill kernel
 # ---------------------------------------------------------------------------
 
-def sdpa_f16(query, key, value, output, scale: float, causal: bool, stream=None) -> None:
-    """query/output [B, Hq, Lq, 128], key/value [B, Hkv, Lk, 128] float16 CUDA tensors."""
+def sdpa_f16(query, key, value, output, scale: float, causal: bool, stream=None,
+             mask=None) -> None:
+    """query/output [B, Hq, Lq, 128], key/value [B, Hkv, Lk, 128] float16 CUDA tensors;
+    mask: None or an additive float16 CUDA tensor [Lq, Lk]."""
     import torch
     B, Hq, Lq, d = query.shape
     Hkv, Lk = key.shape[1], key.shape[2]
     n = load().pkv_sdpa_workspace_bytes(B, Hq, Hkv, Lq, Lk)
     ws = torch.empty(n, dtype=torch.uint8, device=query.device)
-    _call("pkv_sdpa_f16", query.data_ptr(), key.data_ptr(), value.data_ptr(), output.data_ptr(),
-          B, Hq, Hkv, Lq, Lk, ctypes.c_float(scale), int(causal), ws.data_ptr(), n,
-          _stream_ptr(stream))
+    _call("pkv_sdpa_f16", query.data_ptr(), key.data_ptr(), value.data_ptr(),
+          None if mask is None else mask.data_ptr(), output.data_ptr(), B, Hq, Hkv, Lq, Lk,
+          ctypes.c_float(scale), int(causal), ws.data_ptr(), n, _stream_ptr(stream))
 
 
 def sdpa_f16_host(query, key, value, scale: float, causal: bool, mask=None):

@@ -11,12 +11,17 @@
 //     each sequence is copied to a whole number of 16-row pages;
 //   * the group's query heads go to a token-major [rows][G][128] buffer and
 //     the output comes back the same way (two transpose kernels);
-//   * the causal rule key > query + (kv_len - q_len) is the prefill kernel's
-//     own, so q_len <= kv_len is required.
-// head_dim = value_dim = 128; additive masks are not taken (the call fails).
+//   * the causal rule key > query + max(kv_len - q_len, 0) is the prefill
+//     kernel's own (in dense mode, which lets q_len exceed kv_len);
+//   * an additive FP16 mask [q_len][kv_len] (shared by every batch and head,
+//     as the SDK's) is added to the scaled scores inside the kernel's softmax;
+//     a row whose maximum is not finite gives zeros (the CUDA backend's rule,
+//     softmax_rows_kernel, attention_cuda.cu:45-55).
+// head_dim = value_dim = 128.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "pkv_b200.h"
@@ -115,10 +120,11 @@ size_t pkv_sdpa_workspace_bytes(size_t batch, size_t q_heads, size_t kv_heads, s
     return pkv::dense_layout(batch, q_heads, kv_heads, q_len, kv_len).total;
 }
 
-int pkv_sdpa_f16(const void *query, const void *key, const void *value, void *output,
-                 size_t batch, size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
-                 float scale, int causal, void *workspace, size_t workspace_bytes,
-                 PkvStream stream, char *error, size_t error_capacity) {
+int pkv_sdpa_f16(const void *query, const void *key, const void *value,
+                 const void *additive_mask, void *output, size_t batch, size_t q_heads,
+                 size_t kv_heads, size_t q_len, size_t kv_len, float scale, int causal,
+                 void *workspace, size_t workspace_bytes, PkvStream stream, char *error,
+                 size_t error_capacity) {
     using namespace pkv;
     const char *what = "pkv_sdpa_f16";
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
@@ -127,11 +133,13 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value, void *ou
         return 0;
     }
     if (batch == 0 || q_heads == 0 || kv_heads == 0 || q_len == 0 || kv_len == 0 ||
-        q_heads % kv_heads != 0 || q_heads / kv_heads > 65535 || q_len > kv_len ||
+        q_heads % kv_heads != 0 || q_heads / kv_heads > 65535 || q_len > (1u << 30) ||
         kv_len > (1u << 30) || batch * kv_heads > (1u << 24) ||
-        batch * q_heads * q_len >= (size_t(1) << 31) || (causal != 0 && causal != 1)) {
+        batch * q_heads * q_len >= (size_t(1) << 31) || (causal != 0 && causal != 1) ||
+        !isfinite(scale)) {
         pkv_internal_set_error(error, error_capacity,
-                               "%s: needs q_heads a multiple of kv_heads and q_len <= kv_len",
+                               "%s: needs q_heads a multiple of kv_heads, a finite scale and "
+                               "causal 0 or 1",
                                what);
         return 0;
     }
@@ -189,9 +197,11 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value, void *ou
     b.table_stride = (size_t)pages;
     b.seq_lens = lens;
     b.batch = (size_t)S;
-    if (!pkv_paged_prefill(&layer, &b, (size_t)G, offs, qrows, (size_t)(S * (int64_t)q_len),
-                           q_len, scale, causal, orows, PKV_DTYPE_F16, stream, error,
-                           error_capacity))
+    if (!pkv_internal_paged_prefill_ex(&layer, &b, (size_t)G, offs, qrows,
+                                       (size_t)(S * (int64_t)q_len), q_len, scale, causal, orows,
+                                       PKV_DTYPE_F16, static_cast<const uint16_t *>(additive_mask),
+                                       kv_len, q_len > kv_len, stream, error, error_capacity,
+                                       what))
         return 0;
     regroup_kernel<<<grid_for(qn), 256, 0, s>>>(orows, static_cast<uint4 *>(output),
                                                  (int64_t)batch, (int)q_heads, G, (int)q_len,
@@ -210,9 +220,8 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
                       int causal) {
     using namespace pkv;
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
-        additive_mask != nullptr || head_dim != kDHead || value_dim != kDHead ||
-        batch == 0 || query_heads == 0 || kv_heads == 0 || query_length == 0 ||
-        kv_length == 0 || query_heads % kv_heads != 0 || query_length > kv_length)
+        head_dim != kDHead || value_dim != kDHead || batch == 0 || query_heads == 0 ||
+        kv_heads == 0 || query_length == 0 || kv_length == 0 || query_heads % kv_heads != 0)
         return 0;
     std::lock_guard<std::mutex> lock(g_host_mutex);
     int dev = 0;
@@ -221,7 +230,8 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
     const size_t kb = batch * kv_heads * kv_length * kDHead * 2;
     const size_t wsb = pkv_sdpa_workspace_bytes(batch, query_heads, kv_heads, query_length,
                                                 kv_length);
-    const size_t need = align256(qb) * 2 + align256(kb) * 2 + wsb;
+    const size_t mb = additive_mask != nullptr ? query_length * kv_length * 2 : 0;
+    const size_t need = align256(qb) * 2 + align256(kb) * 2 + align256(mb) + wsb;
     if (g_host_ws_bytes[dev] < need) {
         if (g_host_ws[dev] != nullptr) cudaFree(g_host_ws[dev]);
         g_host_ws[dev] = nullptr;
@@ -231,14 +241,15 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
     }
     auto *base = static_cast<unsigned char *>(g_host_ws[dev]);
     unsigned char *dq = base, *dout = dq + align256(qb), *dk = dout + align256(qb);
-    unsigned char *dv = dk + align256(kb), *dws = dv + align256(kb);
+    unsigned char *dv = dk + align256(kb), *dm = dv + align256(kb), *dws = dm + align256(mb);
     // the SDK's backends are synchronous and use the default stream
     if (cudaMemcpy(dq, query, qb, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dk, key, kb, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dv, value, kb, cudaMemcpyHostToDevice) != cudaSuccess)
+        cudaMemcpy(dv, value, kb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        (mb != 0 && cudaMemcpy(dm, additive_mask, mb, cudaMemcpyHostToDevice) != cudaSuccess))
         return 0;
-    if (!pkv_sdpa_f16(dq, dk, dv, dout, batch, query_heads, kv_heads, query_length, kv_length,
-                      scale, causal, dws, wsb, nullptr, nullptr, 0))
+    if (!pkv_sdpa_f16(dq, dk, dv, mb != 0 ? dm : nullptr, dout, batch, query_heads, kv_heads,
+                      query_length, kv_length, scale, causal, dws, wsb, nullptr, nullptr, 0))
         return 0;
     return cudaMemcpy(output, dout, qb, cudaMemcpyDeviceToHost) == cudaSuccess;
 }

@@ -77,10 +77,18 @@ struct PfArgs {
     float scale_log2;
     int32_t causal;
     int32_t paired;  // GQA group even: items carry two heads
+    // General instantiation only: an additive FP16 mask [query row of the
+    // chunk][key] (nullptr: none) with its row stride in elements, whether
+    // 16-byte loads may read it, and dense mode (a chunk may be longer than
+    // its keys; the causal offset kv_len - q_len clamps at 0).
+    const uint16_t *mask;
+    int64_t mask_stride;
+    int32_t mask_vec;
+    int32_t dense;
 };
 
 struct Item {
-    int b, h0, g, q0, nrows, L, pos0, ntiles;
+    int b, h0, g, q0, qrel, nrows, L, pos0, ntiles;
     bool bad;
 };
 
@@ -109,10 +117,11 @@ __device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfAr
     I.g = rest / np;
     I.h0 = I.g * group + (rest - I.g * np) * (a.paired ? 2 : 1);
     I.q0 = qstart + qt * kPfTile;
+    I.qrel = qt * kPfTile;
     I.nrows = min(kPfTile, nq - qt * kPfTile);
     I.L = __ldg(a.seq_lens + lo);
-    I.bad = nq > I.L;
-    I.pos0 = I.L - nq + qt * kPfTile;
+    I.bad = nq > I.L && !a.dense;
+    I.pos0 = max(I.L - nq, 0) + qt * kPfTile;
     const int kmax = a.causal ? min(I.L, I.pos0 + I.nrows) : I.L;
     I.ntiles = I.bad ? 0 : (kmax + kPfTile - 1) / kPfTile;
     return I;
@@ -272,7 +281,39 @@ __device__ __forceinline__ void pv_mmas(uint32_t ocol, uint32_t pcol, uint64_t v
     (sm100::mma_f16_ts_at<p_col(KK) + 16, v_step(KK)>(ocol, pcol, vd, idesc, 1u), ...);
 }
 
-template <typename T, typename OT>
+// Adds the mask (times log2 e) to a chunk of 32 scaled scores of keys kc..;
+// keys at or past L read nothing (the length mask covers them).
+__device__ __forceinline__ void add_mask_chunk(uint32_t (&v)[32], const uint16_t *mrow, int kc,
+                                               int L, bool vec) {
+    if (vec && kc + 32 <= L) {
+        uint4 m[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = __ldg(reinterpret_cast<const uint4 *>(mrow + kc) + i);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w[4] = {m[i].x, m[i].y, m[i].z, m[i].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+                v[8 * i + 2 * k] = __float_as_uint(__uint_as_float(v[8 * i + 2 * k]) + f.x * kLog2e);
+                v[8 * i + 2 * k + 1] =
+                    __float_as_uint(__uint_as_float(v[8 * i + 2 * k + 1]) + f.y * kLog2e);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (kc + i < L)
+                v[i] = __float_as_uint(__uint_as_float(v[i]) +
+                                       __half2float(__ushort_as_half(__ldg(mrow + kc + i))) * kLog2e);
+    }
+}
+
+// GEN = false: the paged prefill path (no mask, scale > 0, so the max can be
+// taken over raw scores and scaled once).  GEN = true: scores are scaled (and
+// masked) before the max, any finite scale, and rows whose running max
+// becomes +inf give zeros (the SDK CUDA backend's rule for a non-finite max).
+template <typename T, typename OT, bool GEN>
 __global__ void __launch_bounds__(kPfThreads, 1)
 paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
@@ -490,6 +531,11 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             const int pos = I.pos0 + (row_ok ? r : I.nrows - 1);
             const int limit = a.causal ? min(pos + 1, I.L) : I.L;  // keys < limit attend
             float m_run = -INFINITY, l = 0.f;
+            bool dead = false;  // GEN: the row's max reached +inf
+            const uint16_t *mrow =
+                GEN && a.mask != nullptr
+                    ? a.mask + (int64_t)(I.qrel + (row_ok ? r : I.nrows - 1)) * a.mask_stride
+                    : nullptr;
             for (int jt = 0; jt < I.ntiles; ++jt, ++jj) {
                 const int k0 = jt * kPfTile;
                 const bool masked = k0 + kPfTile > limit;
@@ -501,6 +547,15 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
 #pragma unroll
                 for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(scol + c * 32, v[c]);
                 tmem_wait_ld();
+                if constexpr (GEN) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            v[c][i] = __float_as_uint(__uint_as_float(v[c][i]) * a.scale_log2);
+                        if (mrow != nullptr) add_mask_chunk(v[c], mrow, k0 + c * 32, I.L, a.mask_vec);
+                    }
+                }
                 if (masked) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) mask_chunk(v[c], k0 + c * 32, limit);
@@ -516,7 +571,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     mc[c] = fmaxf(mc[c], __uint_as_float(v[c][31]));
                 }
                 float mx = max3(mc[0], mc[1], fmaxf(mc[2], mc[3]));
-                mx *= a.scale_log2;  // scale > 0 commutes with max
+                if constexpr (!GEN) mx *= a.scale_log2;  // scale > 0 commutes with max
                 float alpha = 1.f;
                 bool rescale = false;
                 if (mx > m_run + kRescaleThreshold) {  // first tile: m_run = -inf
@@ -557,8 +612,23 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 }
                 // P = exp2(s * scale - m) chunk by chunk into the chunk's own
                 // columns, as a 16-bit high half and the low remainder
-                const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
-                const float2 nm2 = make_float2(-m_run, -m_run);
+                const float sc = GEN ? 1.f : a.scale_log2;
+                const float2 sc2 = make_float2(sc, sc);
+                // GEN: a row that has seen only -inf keeps m = -inf (use 0: its
+                // P is 0); one whose max is +inf is dead (P = 0, output 0)
+                float nm = -m_run;
+                if constexpr (GEN) {
+                    dead = dead || m_run == INFINITY;
+                    nm = m_run == -INFINITY ? 0.f : nm;
+                    if (dead) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[c][i] = 0xff800000u;
+                        nm = 0.f;
+                    }
+                }
+                const float2 nm2 = make_float2(nm, nm);
                 const float2 neg1 = make_float2(-1.f, -1.f);
                 float2 lsum2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -589,7 +659,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 break;
             }
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+            const float inv = l > 0.f && !dead ? 1.f / l : 0.f;
             OT *orow = static_cast<OT *>(a.out) + ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -632,10 +702,10 @@ int sms() {
     return g_sms[dev];
 }
 
-template <typename T, typename OT>
+template <typename T, typename OT, bool GEN>
 int launch(const PfArgs &args, const CUtensorMap &qm, const CUtensorMap &km,
            const CUtensorMap &vm, cudaStream_t s) {
-    auto kern = paged_prefill_tc_kernel<T, OT>;
+    auto kern = paged_prefill_tc_kernel<T, OT, GEN>;
     static int configured[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -659,7 +729,19 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
                       size_t max_query_len, float scale, int causal, void *output,
                       PkvDType output_dtype, PkvStream stream, char *error,
                       size_t error_capacity) {
-    const char *what = "pkv_paged_prefill";
+    return pkv_internal_paged_prefill_ex(layer, batch, q_heads, query_offsets, query,
+                                         total_query_rows, max_query_len, scale, causal, output,
+                                         output_dtype, nullptr, 0, 0, stream, error,
+                                         error_capacity, "pkv_paged_prefill");
+}
+
+int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *batch,
+                                  size_t q_heads, const int32_t *query_offsets, const void *query,
+                                  size_t total_query_rows, size_t max_query_len, float scale,
+                                  int causal, void *output, PkvDType output_dtype,
+                                  const uint16_t *mask, size_t mask_stride, int dense,
+                                  PkvStream stream, char *error, size_t error_capacity,
+                                  const char *what) {
     if (layer == nullptr || batch == nullptr || query_offsets == nullptr || query == nullptr ||
         output == nullptr || layer->key_pool == nullptr || layer->value_pool == nullptr ||
         batch->block_tables == nullptr || batch->seq_lens == nullptr) {
@@ -740,6 +822,13 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
     args.scale_log2 = scale * pkv::kLog2e;
     args.causal = causal;
     args.paired = ((q_heads / kvh) % 2) == 0;
+    args.mask = mask;
+    args.mask_stride = (int64_t)mask_stride;
+    args.mask_vec = mask != nullptr && (uintptr_t)mask % 16 == 0 && mask_stride % 8 == 0;
+    args.dense = dense != 0;
+    // the general instantiation: a mask, or a scale <= 0 (the max is then
+    // taken after scaling); dense mode works in both
+    const bool gen = mask != nullptr || !(scale > 0.f);
     const cudaStream_t s = (cudaStream_t)stream;
     int ok = 1;
     for (size_t b0 = 0; ok && b0 < batch->batch; b0 += pkv::kPfMaxBatch) {
@@ -752,12 +841,17 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
         sl.q_offsets = query_offsets + b0;  // absolute row offsets: query/out stay global
         sl.out = output;
         if (!bf16)
-            ok = output_dtype == PKV_DTYPE_F32 ? pkv::launch<__half, float>(sl, qm, km, vm, s)
-                                               : pkv::launch<__half, __half>(sl, qm, km, vm, s);
+            ok = output_dtype == PKV_DTYPE_F32
+                     ? (gen ? pkv::launch<__half, float, true>(sl, qm, km, vm, s)
+                            : pkv::launch<__half, float, false>(sl, qm, km, vm, s))
+                     : (gen ? pkv::launch<__half, __half, true>(sl, qm, km, vm, s)
+                            : pkv::launch<__half, __half, false>(sl, qm, km, vm, s));
         else
             ok = output_dtype == PKV_DTYPE_F32
-                     ? pkv::launch<__nv_bfloat16, float>(sl, qm, km, vm, s)
-                     : pkv::launch<__nv_bfloat16, __nv_bfloat16>(sl, qm, km, vm, s);
+                     ? (gen ? pkv::launch<__nv_bfloat16, float, true>(sl, qm, km, vm, s)
+                            : pkv::launch<__nv_bfloat16, float, false>(sl, qm, km, vm, s))
+                     : (gen ? pkv::launch<__nv_bfloat16, __nv_bfloat16, true>(sl, qm, km, vm, s)
+                            : pkv::launch<__nv_bfloat16, __nv_bfloat16, false>(sl, qm, km, vm, s));
     }
     if (!ok) {
         pkv_internal_set_error(error, error_capacity, "%s: launch failed: %s", what,

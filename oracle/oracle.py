@@ -389,9 +389,10 @@ class _Ops(ctypes.Structure):
 _RUN_F16 = ctypes.CFUNCTYPE(_i, _p, _p, _p, _p, _p, _s, _s, _s, _s, _s, _s, _s, _f, _i)
 
 
-def ref_cuda_sdpa_f16(q, k, v, scale: float, causal: bool):
+def ref_cuda_sdpa_f16(q, k, v, scale: float, causal: bool, mask=None):
     """The SDK CUDA backend's run_f16 (dense sdpa, attention_cuda.cu:71-99)
-    on host uint16 arrays; returns the output bits or None."""
+    on host uint16 arrays (mask: None or [Lq, Lk] FP16 bits); returns the
+    output bits or None."""
     lib = ctypes.CDLL(str(REF_CUDA_PATH))
     lib.tensor_attention_cuda_backend.restype = ctypes.POINTER(_Ops)
     ops = lib.tensor_attention_cuda_backend().contents
@@ -399,7 +400,8 @@ def ref_cuda_sdpa_f16(q, k, v, scale: float, causal: bool):
     B, Hq, Lq, d = q.shape
     Hkv, Lk, dv = k.shape[1], k.shape[2], v.shape[3]
     q, k, v = (np.ascontiguousarray(a, dtype=np.uint16) for a in (q, k, v))
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint16)
     out = np.zeros((B, Hq, Lq, dv), dtype=np.uint16)
-    ok = run(q.ctypes.data, k.ctypes.data, v.ctypes.data, None, out.ctypes.data, B, Hq, Hkv, Lq,
-             Lk, d, dv, scale, int(causal))
+    ok = run(q.ctypes.data, k.ctypes.data, v.ctypes.data, None if m is None else m.ctypes.data,
+             out.ctypes.data, B, Hq, Hkv, Lq, Lk, d, dv, scale, int(causal))
     return out if ok else None

@@ -1,10 +1,13 @@
 """GPU parity of the dense FP16 SDPA entry points (pkv_sdpa_f16 with device
 tensors, pkv_sdpa_f16_host in the SDK backend hook's host form) against the
 CPU restatement of the SDK's tensor_sdpa_f32 and, where it was built, the
-SDK's own tensor_sdpa_f32 (within max-abs 2e-3 / max-rel 1e-2 over
-|ref| >= 1e-2).  Covers GQA, causal with q_len < kv_len (offset kv_len -
-q_len), kv_len a multiple of 16 (the tensors are the page pool) or not (the
-rows are copied to whole pages), several batches, and the refused shapes."""
+SDK's own tensor_sdpa_f32 and CUDA run_f16 (within max-abs 2e-3 / max-rel
+1e-2 over |ref| >= 1e-2).  Covers GQA, causal with q_len < kv_len (offset
+kv_len - q_len) and q_len > kv_len (offset 0), kv_len a multiple of 16 (the
+tensors are the page pool) or not (the rows are copied to whole pages),
+several batches, additive masks (finite, -inf entries, fully masked rows,
+row strides that do or do not allow 16-byte loads), a +inf mask entry (the
+CUDA backend's zero row), scales <= 0, and the refused shapes."""
 from __future__ import annotations
 
 import numpy as np
@@ -67,11 +70,110 @@ def test_host_hook_and_sdk_cpu(lib, oracle_mod, cuda):
         check_close(got, want, "host hook vs SDK tensor_sdpa_f32")
 
 
+def make_mask(Lq, Lk, seed, dead_rows=()):
+    """N(0, 2) additive mask with ~10 % -inf entries and fully masked rows."""
+    rng = np.random.default_rng(seed)
+    m = (rng.standard_normal((Lq, Lk)) * 2).astype(np.float16)
+    m[rng.random((Lq, Lk)) < 0.1] = -np.inf
+    for r in dead_rows:
+        m[r] = -np.inf
+    return m
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Lq,Lk,causal", [
+    (2, 8, 2, 100, 300, True),    # kv_len % 8 != 0: scalar mask loads
+    (1, 8, 8, 130, 256, False),   # 16-byte mask loads, no causal mask
+    (1, 4, 1, 200, 136, True),    # q_len > kv_len (causal offset 0)
+    (2, 6, 2, 129, 129, False),   # odd group
+])
+def test_device_entry_with_mask(lib, oracle_mod, cuda, B, Hq, Hkv, Lq, Lk, causal):
+    import torch
+    q, k, v = case(B, Hq, Hkv, Lq, Lk, seed=B * 7000 + Lq)
+    mask = make_mask(Lq, Lk, seed=Lq + Lk, dead_rows=(3, Lq - 1))
+    scale = 1 / np.sqrt(128)
+    dq, dk, dv = (torch.from_numpy(a).to(cuda) for a in (q, k, v))
+    dm = torch.from_numpy(mask).to(cuda)
+    out = torch.empty_like(dq)
+    P.sdpa_f16(dq, dk, dv, out, scale, causal, mask=dm)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    want = oracle_mod.sdpa_f32(q.astype(np.float32), k.astype(np.float32),
+                               v.astype(np.float32), scale, causal, mask=mask.astype(np.float32))
+    check_close(got, want, f"masked B={B} Hq={Hq} Hkv={Hkv} Lq={Lq} Lk={Lk} causal={causal}")
+    assert not got[:, :, 3].any() and not got[:, :, Lq - 1].any()  # fully masked rows
+    assert P.device_fault(0) == 0
+
+
+@pytest.mark.parametrize("Lq,Lk,causal", [(300, 100, True), (300, 100, False)])
+def test_device_entry_q_longer_than_kv(lib, oracle_mod, cuda, Lq, Lk, causal):
+    import torch
+    q, k, v = case(1, 8, 2, Lq, Lk, seed=Lq * 3 + Lk)
+    scale = 1 / np.sqrt(128)
+    dq, dk, dv = (torch.from_numpy(a).to(cuda) for a in (q, k, v))
+    out = torch.empty_like(dq)
+    P.sdpa_f16(dq, dk, dv, out, scale, causal)
+    torch.cuda.synchronize()
+    check_close(out.float().cpu().numpy(), expected(q, k, v, scale, causal, oracle_mod),
+                f"Lq={Lq} > Lk={Lk} causal={causal}")
+
+
+@pytest.mark.parametrize("scale", [-0.09, 0.0])
+def test_device_entry_nonpositive_scale(lib, oracle_mod, cuda, scale):
+    import torch
+    q, k, v = case(1, 8, 2, 64, 200, seed=5)
+    dq, dk, dv = (torch.from_numpy(a).to(cuda) for a in (q, k, v))
+    out = torch.empty_like(dq)
+    P.sdpa_f16(dq, dk, dv, out, scale, True)
+    torch.cuda.synchronize()
+    check_close(out.float().cpu().numpy(), expected(q, k, v, scale, True, oracle_mod),
+                f"scale {scale}")
+
+
+def test_host_hook_with_mask(lib, oracle_mod, cuda):
+    q, k, v = case(2, 8, 4, 64, 200, seed=8)
+    mask = make_mask(64, 200, seed=9, dead_rows=(10,))
+    got = P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1, True,
+                          mask=mask.view(np.uint16))
+    assert got is not None
+    got = got.view(np.float16).astype(np.float32)
+    want = oracle_mod.sdpa_f32(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
+                               0.1, True, mask=mask.astype(np.float32))
+    check_close(got, want, "host hook with mask vs oracle")
+    if O.ref_cuda_available():
+        ref = O.ref_cuda_sdpa_f16(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1,
+                                  True, mask=mask.view(np.uint16))
+        assert ref is not None
+        check_close(got, ref.view(np.float16).astype(np.float32), "host hook vs SDK CUDA sdpa")
+    if O.ref_available():
+        want = O.ref_sdpa_f32(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32),
+                              0.1, True, mask=mask.astype(np.float32))
+        check_close(got, want, "host hook vs SDK tensor_sdpa_f32 (mask)")
+
+
+def test_positive_infinite_mask_row(lib, oracle_mod, cuda):
+    """A +inf mask entry makes that row's maximum non-finite: zeros, as the
+    SDK CUDA backend's softmax_rows_kernel gives (its CPU path would instead
+    spread the row uniformly over the +inf keys)."""
+    q, k, v = case(1, 4, 2, 16, 64, seed=12)
+    mask = np.zeros((16, 64), np.float16)
+    mask[5, 7] = np.inf
+    got = P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1, False,
+                          mask=mask.view(np.uint16))
+    assert got is not None
+    got = got.view(np.float16).astype(np.float32)
+    assert not got[:, :, 5].any()
+    rows = [r for r in range(16) if r != 5]
+    want = expected(q, k, v, 0.1, False, oracle_mod)
+    check_close(got[:, :, rows], want[:, :, rows], "rows without +inf")
+    if O.ref_cuda_available():
+        ref = O.ref_cuda_sdpa_f16(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1,
+                                  False, mask=mask.view(np.uint16))
+        assert ref is not None and not ref.view(np.float16)[:, :, 5].astype(np.float32).any()
+
+
 def test_refused_shapes(lib, cuda):
-    q, k, v = case(1, 4, 2, 32, 16, seed=1)  # q_len > kv_len
-    assert P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1,
-                           True) is None
-    q, k, v = case(1, 4, 2, 8, 16, seed=2)
-    mask = np.zeros((8, 16), np.float16).view(np.uint16)
-    assert P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1, True,
-                           mask=mask) is None
+    q, k, v = case(1, 4, 2, 32, 16, seed=1)
+    q64 = np.ascontiguousarray(q[..., :64])
+    k64, v64 = np.ascontiguousarray(k[..., :64]), np.ascontiguousarray(v[..., :64])
+    assert P.sdpa_f16_host(q64.view(np.uint16), k64.view(np.uint16), v64.view(np.uint16), 0.1,
+                           True) is None  # head_dim 64

@@ -47,17 +47,17 @@ class PrefillCase:
         self.d_len = torch.from_numpy(self.lengths.astype(np.int32)).to(device)
         self.d_offs = torch.from_numpy(self.offs).to(device)
 
-    def run(self, causal=True, out_dtype=None):
+    def run(self, causal=True, out_dtype=None, scale=1 / np.sqrt(128)):
         import torch
         out = torch.full((int(self.offs[-1]), self.q_heads, 128), float("nan"),
                          dtype=out_dtype or torch.float32, device=self.device)
         layer = P.make_layer(self.d_k, self.d_v, self.bs, self.kv_heads, 128)
         P.paged_prefill(layer, P.make_batch(self.d_tab, self.d_len), self.d_q, self.d_offs, out,
-                        1 / np.sqrt(128), int(self.chunk.max()), causal)
+                        scale, int(self.chunk.max()), causal)
         torch.cuda.synchronize()
         return out.float().cpu().numpy()
 
-    def oracle(self, oracle_mod, causal=True, rows=None):
+    def oracle(self, oracle_mod, causal=True, rows=None, scale=1 / np.sqrt(128)):
         want = np.zeros((int(self.offs[-1]), self.q_heads, 128), np.float32)
         for b in range(len(self.lengths)):
             sel = np.arange(self.offs[b], self.offs[b + 1]) if rows is None else \
@@ -67,7 +67,7 @@ class PrefillCase:
             pos = self.past[b] + (sel - self.offs[b])
             want[sel] = oracle_mod.paged_attention_rows(
                 self.q[sel], pos, causal, self.dtype, self.kpool, self.vpool, self.kv_heads, 128,
-                self.bs, self.tables[b], int(self.lengths[b]), float(1 / np.sqrt(128)))
+                self.bs, self.tables[b], int(self.lengths[b]), float(scale))
         return want
 
 
@@ -90,6 +90,16 @@ def test_prefill_matches_oracle(lib, oracle_mod, cuda, dtype, causal, group):
                        seed=10 + group, device=cuda)
     got = case.run(causal)
     check_close(got, case.oracle(oracle_mod, causal), f"{dtype} causal={causal} group={group}")
+    assert P.device_fault(0) == 0
+
+
+@pytest.mark.parametrize("scale", [-0.12, 0.0])
+def test_prefill_nonpositive_scale(lib, oracle_mod, cuda, scale):
+    """A scale <= 0 (allowed by the SDK: any finite scale) takes the general
+    instantiation, which scales before the row max."""
+    case = PrefillCase([0, 300], [200, 129], 8, 2, "bf16", seed=21, device=cuda)
+    got = case.run(True, scale=scale)
+    check_close(got, case.oracle(oracle_mod, True, scale=scale), f"scale {scale}")
     assert P.device_fault(0) == 0
 
 
