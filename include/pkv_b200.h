@@ -169,6 +169,13 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch,
 int pkv_device_fault(int device, uint32_t *code, char *error,
                      size_t error_capacity);
 
+/* Self-test of the failure path the kernels rely on (synchronises the
+ * current device, takes about half a second): a one-CTA kernel holding TMEM
+ * waits on an mbarrier nothing arrives on; the bounded wait gives up, the CTA
+ * frees TMEM and exits.  *code receives the recorded fault code -- 4
+ * (wait timeout) when the bounded wait works.  The device stays usable. */
+int pkv_selftest_wait_timeout(uint32_t *code, char *error, size_t error_capacity);
+
 /* Dense FP16 SDPA on the tcgen05 prefill kernel: query [batch][q_heads]
  * [q_len][128], key/value [batch][kv_heads][kv_len][128], output like query,
  * optional additive mask [q_len][kv_len] (NULL: none; shared by every batch

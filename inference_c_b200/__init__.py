@@ -142,6 +142,7 @@ EXPORTS = {
     "pkv_paged_prefill": (_c_int, [_LP, _BP, _c_size, _c_ptr, _c_ptr, _c_size, _c_size,
                                    ctypes.c_float, _c_int, _c_ptr, _c_int, _c_ptr, *_ERR]),
     "pkv_device_fault": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_uint32), *_ERR]),
+    "pkv_selftest_wait_timeout": (_c_int, [ctypes.POINTER(ctypes.c_uint32), *_ERR]),
     "pkv_sdpa_workspace_bytes": (_c_size, [_c_size, _c_size, _c_size, _c_size, _c_size]),
     "pkv_sdpa_f16": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size, _c_size,
                               _c_size, _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size, _c_ptr,
@@ -372,6 +373,14 @@ def paged_prefill(layer: PkvPagedLayer, batch: PkvBatch, query, query_offsets, o
 def device_fault(device: int = 0) -> int:
     code = ctypes.c_uint32(0)
     _call("pkv_device_fault", device, ctypes.byref(code))
+    return code.value
+
+
+def selftest_wait_timeout() -> int:
+    """Runs the bounded-wait self-test on the current device; returns the
+    fault code it recorded (4: the wait gave up as designed)."""
+    code = ctypes.c_uint32(0)
+    _call("pkv_selftest_wait_timeout", ctypes.byref(code))
     return code.value
 
 

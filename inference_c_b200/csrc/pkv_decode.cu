@@ -1555,3 +1555,67 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
                             max_seq_len, 0, scratch, kDecodeStaticScratchBytes, stream, error,
                             error_capacity);
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded waits (the failure path every warp-specialised
+// kernel here relies on), run on the GPU without faulting it: one CTA holds
+// TMEM, one warp waits on an mbarrier that nothing arrives on, the wait gives
+// up after its cycle budget, raises the CTA's abort flag and records
+// kFaultWaitTimeout, and the CTA frees TMEM and exits -- the context stays
+// usable.
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ uint32_t g_selftest_word;
+
+__global__ void __launch_bounds__(64) selftest_wait_kernel() {
+    using namespace pkv::sm100;
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_slot, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        // phase 0 of a fresh barrier with one expected arrival never completes
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar, 0, &abort_flag, &g_selftest_word));
+        if (ok && (threadIdx.x & 31) == 0) g_selftest_word = 0xffffffffu;  // cannot happen
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem_slot, 32);
+}
+
+}  // namespace
+
+extern "C" int pkv_selftest_wait_timeout(uint32_t *code, char *error, size_t error_capacity) {
+    const char *what = "pkv_selftest_wait_timeout";
+    if (code == nullptr) {
+        pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    const uint32_t zero = 0;
+    cudaError_t st = cudaMemcpyToSymbol(g_selftest_word, &zero, sizeof zero);
+    if (st == cudaSuccess) {
+        selftest_wait_kernel<<<1, 64>>>();
+        st = cudaGetLastError();
+    }
+    if (st == cudaSuccess) st = cudaDeviceSynchronize();
+    if (st == cudaSuccess) st = cudaMemcpyFromSymbol(code, g_selftest_word, sizeof *code);
+    if (st != cudaSuccess) {
+        pkv_internal_set_error(error, error_capacity, "%s: %s", what, cudaGetErrorString(st));
+        return 0;
+    }
+    return 1;
+}
