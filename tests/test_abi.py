@@ -111,6 +111,35 @@ def test_kernel_entry_points_reject_bad_arguments(lib):
     assert lib.pkv_step_end(None, 1, e, len(e)) == 0
 
 
+def test_dense_and_selftest_entry_points_reject_bad_arguments(lib):
+    """Validation that happens before any device work (no GPU needed)."""
+    e = _err()
+    assert lib.pkv_sdpa_f16(None, None, None, None, None, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 1,
+                            None, 0, None, e, len(e)) == 0
+    assert b"null" in e.value
+    e = _err()  # q_heads not a multiple of kv_heads
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 6, 4, 4, 4, ctypes.c_float(0.1), 1, 256,
+                            1 << 20, None, e, len(e)) == 0
+    assert b"multiple" in e.value
+    e = _err()  # non-finite scale
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(float("inf")), 1,
+                            256, 1 << 20, None, e, len(e)) == 0
+    assert b"finite" in e.value
+    e = _err()  # causal must be 0 or 1
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 2, 256,
+                            1 << 20, None, e, len(e)) == 0
+    e = _err()  # workspace too small
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 1, 256, 8,
+                            None, e, len(e)) == 0
+    assert b"workspace" in e.value
+    # the host hook refuses head_dim / value_dim other than 128 (returns 0)
+    assert lib.pkv_sdpa_f16_host(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 64, 64, ctypes.c_float(0.1),
+                                 1) == 0
+    e = _err()
+    assert lib.pkv_selftest_wait_timeout(None, e, len(e)) == 0
+    assert b"null" in e.value
+
+
 def test_workspace_size_is_monotonic(lib):
     small = lib.pkv_decode_workspace_bytes(1, 8, 64, 512, 0)
     big = lib.pkv_decode_workspace_bytes(32, 32, 128, 4096, 0)
