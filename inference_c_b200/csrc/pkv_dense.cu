@@ -9,8 +9,9 @@
 //     pool with one KV head whose pages are consecutive; when kv_len is a
 //     multiple of 16 the tensors themselves are the pool (no copy), otherwise
 //     each sequence is copied to a whole number of 16-row pages;
-//   * the group's query heads go to a token-major [rows][G][128] buffer and
-//     the output comes back the same way (two transpose kernels);
+//   * the query and output tensors are read and written in place: the
+//     kernel's dense layout addresses head (b, h) row i at ((b*Hq + h)*Lq +
+//     i)*128, the group of KV head g being heads g*G .. g*G+G-1;
 //   * the causal rule key > query + max(kv_len - q_len, 0) is the prefill
 //     kernel's own (in dense mode, which lets q_len exceed kv_len);
 //   * an additive FP16 mask [q_len][kv_len] (shared by every batch and head,
@@ -33,26 +34,6 @@ namespace {
 constexpr int kDHead = 128;
 constexpr int kPage = 16;
 constexpr int kChunks = kDHead / 8;  // 16-byte chunks per row
-
-// Q [B][Hq][Lq][128] -> Q' [(b*Hkv + g)*Lq + i][j][128], h = g*G + j (and back).
-__global__ void regroup_kernel(const uint4 *src, uint4 *dst, int64_t B, int Hq, int G, int Lq,
-                               bool to_rows) {
-    const int64_t n = B * Hq * (int64_t)Lq * kChunks;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(e % kChunks);
-        int64_t r = e / kChunks;
-        const int i = (int)(r % Lq);
-        r /= Lq;
-        const int h = (int)(r % Hq);
-        const int64_t b = r / Hq;
-        const int g = h / G, j = h - g * G;
-        const int64_t dense = ((b * Hq + h) * Lq + i) * kChunks + c;
-        const int64_t rows = (((b * (Hq / G) + g) * Lq + i) * G + j) * kChunks + c;
-        if (to_rows) dst[rows] = src[dense];
-        else dst[dense] = src[rows];
-    }
-}
 
 // K or V of every (b, g) into a whole number of 16-row pages.
 __global__ void pad_rows_kernel(const uint4 *src, uint4 *dst, int64_t S, int Lk, int pages) {
@@ -83,16 +64,14 @@ __global__ void tables_kernel(uint32_t *tables, int32_t *lens, int32_t *offs, in
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 struct DenseLayout {
-    size_t qrows, orows, tables, lens, offs, kpad, vpad, total;
+    size_t tables, lens, offs, kpad, vpad, total;
 };
 
 DenseLayout dense_layout(size_t B, size_t Hq, size_t Hkv, size_t Lq, size_t Lk) {
     const size_t S = B * Hkv, pages = (Lk + kPage - 1) / kPage;
     const bool pad = Lk % kPage != 0;
     DenseLayout w;
-    w.qrows = 0;
-    w.orows = align256(B * Hq * Lq * kDHead * 2);
-    w.tables = w.orows + align256(B * Hq * Lq * kDHead * 2);
+    w.tables = 0;
     w.lens = w.tables + align256(S * pages * 4);
     w.offs = w.lens + align256(S * 4);
     w.kpad = w.offs + align256((S + 1) * 4);
@@ -157,16 +136,10 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
     const int G = (int)(q_heads / kv_heads);
     const int pages = (int)((kv_len + kPage - 1) / kPage);
     const bool pad = kv_len % kPage != 0;
-    auto *qrows = reinterpret_cast<uint4 *>(ws + w.qrows);
-    auto *orows = reinterpret_cast<uint4 *>(ws + w.orows);
     auto *tables = reinterpret_cast<uint32_t *>(ws + w.tables);
     auto *lens = reinterpret_cast<int32_t *>(ws + w.lens);
     auto *offs = reinterpret_cast<int32_t *>(ws + w.offs);
     const void *kpool = key, *vpool = value;
-    const int64_t qn = (int64_t)(batch * q_heads * q_len) * kChunks;
-    regroup_kernel<<<grid_for(qn), 256, 0, s>>>(static_cast<const uint4 *>(query), qrows,
-                                                 (int64_t)batch, (int)q_heads, G, (int)q_len,
-                                                 true);
     tables_kernel<<<grid_for(S * pages + S + 1), 256, 0, s>>>(tables, lens, offs, S, pages,
                                                               (int)kv_len, (int)q_len);
     if (pad) {
@@ -197,20 +170,11 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
     b.table_stride = (size_t)pages;
     b.seq_lens = lens;
     b.batch = (size_t)S;
-    if (!pkv_internal_paged_prefill_ex(&layer, &b, (size_t)G, offs, qrows,
-                                       (size_t)(S * (int64_t)q_len), q_len, scale, causal, orows,
-                                       PKV_DTYPE_F16, static_cast<const uint16_t *>(additive_mask),
-                                       kv_len, q_len > kv_len, stream, error, error_capacity,
-                                       what))
-        return 0;
-    regroup_kernel<<<grid_for(qn), 256, 0, s>>>(orows, static_cast<uint4 *>(output),
-                                                 (int64_t)batch, (int)q_heads, G, (int)q_len,
-                                                 false);
-    if (cudaGetLastError() != cudaSuccess) {
-        pkv_internal_set_error(error, error_capacity, "%s: launch failed", what);
-        return 0;
-    }
-    return 1;
+    return pkv_internal_paged_prefill_ex(&layer, &b, (size_t)G, offs, query,
+                                         (size_t)(S * (int64_t)q_len), q_len, scale, causal,
+                                         output, PKV_DTYPE_F16,
+                                         static_cast<const uint16_t *>(additive_mask), kv_len,
+                                         q_len > kv_len, 1, stream, error, error_capacity, what);
 }
 
 int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t *value,

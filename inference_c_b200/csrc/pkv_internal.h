@@ -46,16 +46,18 @@ int pkv_internal_take_sequence_fault(uint32_t *code);
 
 /* pkv_paged_prefill with the general options the dense SDPA needs: an
  * additive FP16 mask [query row of the chunk][key] with a row stride in
- * elements (NULL: none), and dense mode (a chunk may be longer than its
- * sequence; the causal offset kv_len - q_len clamps at 0).  Errors name
- * `what`. */
+ * elements (NULL: none), dense mode (a chunk may be longer than its
+ * sequence; the causal offset kv_len - q_len clamps at 0), and the dense
+ * layout (query and output are [sequences * q_heads][max_query_len][128],
+ * every sequence holding max_query_len rows, read and written in place).
+ * Errors name `what`. */
 int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *batch,
                                   size_t q_heads, const int32_t *query_offsets, const void *query,
                                   size_t total_query_rows, size_t max_query_len, float scale,
                                   int causal, void *output, PkvDType output_dtype,
                                   const uint16_t *mask, size_t mask_stride, int dense,
-                                  PkvStream stream, char *error, size_t error_capacity,
-                                  const char *what);
+                                  int dense_layout, PkvStream stream, char *error,
+                                  size_t error_capacity, const char *what);
 
 /* Writes a message into a caller error buffer (NULL-safe). */
 void pkv_internal_set_error(char *error, size_t capacity, const char *fmt, ...);

@@ -85,6 +85,11 @@ struct PfArgs {
     int64_t mask_stride;
     int32_t mask_vec;
     int32_t dense;
+    // Dense layout (the SDK's [batch][heads][rows][128] tensors): sequence s
+    // holds rows [0, dense_rows) of query/output heads s*q_heads .. +q_heads-1,
+    // read and written in place instead of token-major rows.
+    int32_t dense_layout;
+    int32_t dense_rows;
 };
 
 struct Item {
@@ -387,11 +392,15 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             if (!mbar_wait(q_empty, (qi & 1) ^ 1, abort_flag, fault)) break;
             if (lane == 0) {
                 mbar_arrive_expect_tx(q_full, (paired ? 4u : 2u) * kHalf);
-                tma_load_3d(sm + kQOff, &qmap, q_full, 0, I.h0, I.q0);
-                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, I.h0, I.q0);
+                // token-major rows: (column, head, row); dense: (column, row, head)
+                const int32_t c1 = a.dense_layout ? I.qrel : I.h0;
+                const int32_t c2 = a.dense_layout ? I.b * a.q_heads + I.h0 : I.q0;
+                const int32_t d1 = a.dense_layout ? 0 : 1, d2 = a.dense_layout ? 1 : 0;
+                tma_load_3d(sm + kQOff, &qmap, q_full, 0, c1, c2);
+                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, c1, c2);
                 if (paired) {
-                    tma_load_3d(sm + kQOff + 2 * kHalf, &qmap, q_full, 0, I.h0 + 1, I.q0);
-                    tma_load_3d(sm + kQOff + 3 * kHalf, &qmap, q_full, 64, I.h0 + 1, I.q0);
+                    tma_load_3d(sm + kQOff + 2 * kHalf, &qmap, q_full, 0, c1 + d1, c2 + d2);
+                    tma_load_3d(sm + kQOff + 3 * kHalf, &qmap, q_full, 64, c1 + d1, c2 + d2);
                 }
             }
             __syncwarp();
@@ -660,7 +669,10 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             }
             tc_fence_after();
             const float inv = l > 0.f && !dead ? 1.f / l : 0.f;
-            OT *orow = static_cast<OT *>(a.out) + ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128;
+            OT *orow = static_cast<OT *>(a.out) +
+                       (a.dense_layout
+                            ? (((int64_t)I.b * a.q_heads + I.h0 + w) * a.dense_rows + I.qrel + r) * 128
+                            : ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t o[32];
@@ -731,7 +743,7 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
                       size_t error_capacity) {
     return pkv_internal_paged_prefill_ex(layer, batch, q_heads, query_offsets, query,
                                          total_query_rows, max_query_len, scale, causal, output,
-                                         output_dtype, nullptr, 0, 0, stream, error,
+                                         output_dtype, nullptr, 0, 0, 0, stream, error,
                                          error_capacity, "pkv_paged_prefill");
 }
 
@@ -740,8 +752,8 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
                                   size_t total_query_rows, size_t max_query_len, float scale,
                                   int causal, void *output, PkvDType output_dtype,
                                   const uint16_t *mask, size_t mask_stride, int dense,
-                                  PkvStream stream, char *error, size_t error_capacity,
-                                  const char *what) {
+                                  int dense_layout, PkvStream stream, char *error,
+                                  size_t error_capacity, const char *what) {
     if (layer == nullptr || batch == nullptr || query_offsets == nullptr || query == nullptr ||
         output == nullptr || layer->key_pool == nullptr || layer->value_pool == nullptr ||
         batch->block_tables == nullptr || batch->seq_lens == nullptr) {
@@ -790,9 +802,20 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
         bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap qm, km, vm;
     {
+        // token-major [rows][q_heads][128], or dense [sequences * q_heads]
+        // [max_query_len][128] with every sequence holding max_query_len rows
+        const uint64_t nseq_heads = dense_layout ? total_query_rows / max_query_len * q_heads : 0;
         cuuint64_t dims[3] = {128, q_heads, total_query_rows};
         cuuint64_t strides[2] = {256, q_heads * 256};
         cuuint32_t box[3] = {64, 1, 128};
+        if (dense_layout) {
+            dims[1] = max_query_len;
+            dims[2] = nseq_heads;
+            strides[0] = 256;
+            strides[1] = max_query_len * 256;
+            box[1] = 128;
+            box[2] = 1;
+        }
         cuuint32_t es[3] = {1, 1, 1};
         if (enc(&qm, dt, 3, const_cast<void *>(query), dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -826,6 +849,8 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
     args.mask_stride = (int64_t)mask_stride;
     args.mask_vec = mask != nullptr && (uintptr_t)mask % 16 == 0 && mask_stride % 8 == 0;
     args.dense = dense != 0;
+    args.dense_layout = dense_layout != 0;
+    args.dense_rows = (int32_t)max_query_len;
     // the general instantiation: a mask, or a scale <= 0 (the max is then
     // taken after scaling); dense mode works in both
     const bool gen = mask != nullptr || !(scale > 0.f);
