@@ -132,6 +132,20 @@ __device__ __forceinline__ Item item_at(int64_t u, const int *prefix, const PfAr
     return I;
 }
 
+// The k-th item of this CTA: rounds of gridDim.x consecutive items.  Items
+// come longest first within a sequence, so a plain stride gives the first
+// CTAs the longest item of every round; in the dense layout (one long causal
+// sequence per (batch, KV head): item sizes from 1 to q_len/128 key tiles)
+// the CTA order is reversed in every other round, pairing long with short
+// (config 7: the heaviest CTA 74 -> ~58 key tiles against a mean of 57).
+// Paged chunks over a long past have items of similar size and keep the
+// plain stride (measured 0.9 % faster there).
+__device__ __forceinline__ int64_t item_order(int64_t k, bool serpentine) {
+    const int64_t c =
+        serpentine && (k & 1) ? (int64_t)gridDim.x - 1 - blockIdx.x : (int64_t)blockIdx.x;
+    return k * gridDim.x + c;
+}
+
 __device__ void build_item_prefix(const PfArgs &a, int *prefix, int *scratch) {
     const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (a.batch + nthr - 1) / nthr;
@@ -372,6 +386,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int64_t total_items = prefix[a.batch];
+    const bool serp = a.dense_layout != 0;
     uint32_t *fault = &g_prefill_fault;
 
     if (warp < 4) {
@@ -382,7 +397,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
         // ------------------------------ producer ------------------------------
         uint32_t jj = 0, qi = 0;
         bool ok = true;
-        for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
+        for (int64_t k = 0, u = item_order(0, serp); ok && u < total_items;
+             u = item_order(++k, serp)) {
             const Item I = item_at(u, prefix, a);
             if (I.bad) {
                 if (lane == 0) record_fault(fault, kFaultRowsMismatch);
@@ -497,7 +513,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             // Issue order per tile j: paired  S_A(j) PV_B(j-1) S_B(j) PV_A(j);
             //                         unpaired S(j) PV(j-1).
             // Each softmax group works while the tensor pipe serves the other.
-            for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
+            for (int64_t k = 0, u = item_order(0, serp); ok && u < total_items;
+                 u = item_order(++k, serp)) {
                 const Item I = item_at(u, prefix, a);
                 if (I.bad || I.ntiles == 0) continue;
                 if (!mbar_wait(q_full, qi & 1, abort_flag, fault)) break;
@@ -533,7 +550,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
         const uint32_t ocol = tmem + w * 256 + 128 + lane_off;
         uint32_t jj = 0;
         bool ok = true;
-        for (int64_t u = blockIdx.x; ok && u < total_items; u += gridDim.x) {
+        for (int64_t k = 0, u = item_order(0, serp); ok && u < total_items;
+             u = item_order(++k, serp)) {
             const Item I = item_at(u, prefix, a);
             if (I.bad || I.ntiles == 0) continue;
             const bool row_ok = r < I.nrows;
