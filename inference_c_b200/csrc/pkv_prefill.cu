@@ -90,6 +90,7 @@ struct PfArgs {
     // read and written in place instead of token-major rows.
     int32_t dense_layout;
     int32_t dense_rows;
+    int32_t seq0;  // dense layout: the launch's first sequence (launches hold <= kPfMaxBatch)
 };
 
 struct Item {
@@ -410,7 +411,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 mbar_arrive_expect_tx(q_full, (paired ? 4u : 2u) * kHalf);
                 // token-major rows: (column, head, row); dense: (column, row, head)
                 const int32_t c1 = a.dense_layout ? I.qrel : I.h0;
-                const int32_t c2 = a.dense_layout ? I.b * a.q_heads + I.h0 : I.q0;
+                const int32_t c2 = a.dense_layout ? (a.seq0 + I.b) * a.q_heads + I.h0 : I.q0;
                 const int32_t d1 = a.dense_layout ? 0 : 1, d2 = a.dense_layout ? 1 : 0;
                 tma_load_3d(sm + kQOff, &qmap, q_full, 0, c1, c2);
                 tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, c1, c2);
@@ -689,7 +690,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             const float inv = l > 0.f && !dead ? 1.f / l : 0.f;
             OT *orow = static_cast<OT *>(a.out) +
                        (a.dense_layout
-                            ? (((int64_t)I.b * a.q_heads + I.h0 + w) * a.dense_rows + I.qrel + r) * 128
+                            ? (((int64_t)(a.seq0 + I.b) * a.q_heads + I.h0 + w) * a.dense_rows +
+                               I.qrel + r) * 128
                             : ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -869,6 +871,7 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
     args.dense = dense != 0;
     args.dense_layout = dense_layout != 0;
     args.dense_rows = (int32_t)max_query_len;
+    args.seq0 = 0;
     // the general instantiation: a mask, or a scale <= 0 (the max is then
     // taken after scaling); dense mode works in both
     const bool gen = mask != nullptr || !(scale > 0.f);
@@ -879,6 +882,7 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
                                                                       : (size_t)pkv::kPfMaxBatch;
         pkv::PfArgs sl = args;
         sl.batch = (int32_t)n;
+        sl.seq0 = (int32_t)b0;
         sl.tables = batch->block_tables + b0 * batch->table_stride;
         sl.seq_lens = batch->seq_lens + b0;
         sl.q_offsets = query_offsets + b0;  // absolute row offsets: query/out stay global

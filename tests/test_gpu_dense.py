@@ -37,6 +37,7 @@ def expected(q, k, v, scale, causal, oracle_mod):
     (2, 8, 2, 256, 256, True),    # the tensors themselves are the page pool
     (1, 8, 8, 130, 400, False),   # MHA, no causal mask
     (3, 6, 2, 129, 129, True),    # odd group (3 query heads per KV head)
+    (65, 16, 8, 16, 32, True),    # 520 (batch, KV head) sequences: two kernel launches
 ])
 def test_device_entry_matches_oracle(lib, oracle_mod, cuda, B, Hq, Hkv, Lq, Lk, causal):
     import torch
