@@ -1075,8 +1075,8 @@ def run_dense(args) -> None:
         "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s",
                      "frac": value / peak, "traffic": None, "peak_kind": kind,
                      "algorithmic_flops_per_call": flops,
-                     "note": "device entry with resident tensors; includes the two regroup "
-                             "copies around the prefill kernel"},
+                     "note": "device entry with resident tensors (query and output read "
+                             "and written in place by the prefill kernel)"},
         "e2e": {"value": flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": bytes_h, "d2h_bytes_per_step": q.numel() * 2,
                 "api": "run_f16 backend hook with host tensors (pkv_sdpa_f16_host)"},
