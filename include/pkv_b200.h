@@ -196,7 +196,11 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
 /* The same with host tensors, in the argument order of the SDK backend hook
  * run_f16 (src/attention_backend.h:14-18), so it can be installed as that
  * hook: uploads, computes on the current device, downloads, synchronous.
- * Returns 0 for head_dim/value_dim other than 128. */
+ * Returns 0 for head_dim/value_dim other than 128.  Its first call allocates,
+ * and keeps until exit, a device buffer sized for the largest call so far
+ * and 32 MiB of pinned host memory (two staging buffers that up to 8 host
+ * threads fill while the DMA engine moves the other); calls are serialised
+ * internally. */
 int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key,
                       const uint16_t *value, const uint16_t *additive_mask,
                       uint16_t *output, size_t batch, size_t query_heads,
