@@ -133,15 +133,21 @@ void par_copy(void *dst, const void *src, size_t n) {
     }
     std::vector<std::thread> ts;
     const size_t part = (n / nt + 63) & ~size_t(63);
-    for (size_t t = 0; t < nt; ++t) {
-        const size_t off = t * part;
-        if (off >= n) break;
-        const size_t len = off + part < n ? part : n - off;
-        ts.emplace_back([=] {
-            std::memcpy(static_cast<unsigned char *>(dst) + off,
-                        static_cast<const unsigned char *>(src) + off, len);
-        });
+    size_t off = 0;
+    try {  // no exception may leave the C ABI: a thread that cannot start
+        ts.reserve(nt);  // leaves its part to this thread
+        for (; off < n && ts.size() + 1 < nt; off += part) {
+            const size_t len = off + part < n ? part : n - off;
+            ts.emplace_back([=] {
+                std::memcpy(static_cast<unsigned char *>(dst) + off,
+                            static_cast<const unsigned char *>(src) + off, len);
+            });
+        }
+    } catch (...) {
     }
+    if (off < n)
+        std::memcpy(static_cast<unsigned char *>(dst) + off,
+                    static_cast<const unsigned char *>(src) + off, n - off);
     for (auto &t : ts) t.join();
 }
 
