@@ -992,7 +992,12 @@ int tensor_attention_decode_sequence_paged(const TensorPagedKVDecodeRequest *req
         l0.head_dim != D.hd || !pkv_pool_layer(pool, D.layers - 1, &l0) ||
         pkv_pool_layer(pool, D.layers, &l0))
         return 0;
-    Context *c = context_for_device(dev);
+    Context *c = nullptr;
+    try {  // the first call on a device adds its context (a host allocation)
+        c = context_for_device(dev);
+    } catch (...) {
+        c = nullptr;
+    }
     if (c == nullptr) return 0;
     size_t current = 0;
     if (!tensor_paged_kv_sequence_length(cache, request->sequence, &current)) return 0;
@@ -1005,10 +1010,17 @@ int tensor_attention_decode_sequence_paged(const TensorPagedKVDecodeRequest *req
     const WF fmt = !quantized ? WF::Dense
                               : (request->weight_quantization == TENSOR_WEIGHT_Q8_0 ? WF::Q8
                                                                                     : WF::Q4);
-    if (ok)
-        ok = request->storage == TENSOR_PAGED_KV_F32
-                 ? run_decoder<float>(request, D, fmt, pool, batch, current, *c)
-                 : run_decoder<__half>(request, D, fmt, pool, batch, current, *c);
+    // no C++ exception (a host allocation failing) may leave this C function
+    // or skip the rollback below
+    if (ok) {
+        try {
+            ok = request->storage == TENSOR_PAGED_KV_F32
+                     ? run_decoder<float>(request, D, fmt, pool, batch, current, *c)
+                     : run_decoder<__half>(request, D, fmt, pool, batch, current, *c);
+        } catch (...) {
+            ok = false;
+        }
+    }
     if (ok) {
         uint32_t fault = 0;
         ok = pkv_device_fault(dev, &fault, nullptr, 0) && fault == 0;
