@@ -115,15 +115,23 @@ int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes,
 
 /* Paged decode SDPA, one query token per sequence, GQA.
  * query/output: [batch][q_heads][head_dim]; output dtype F16, BF16 or F32.
- * Each CTA owns one (sequence, KV head, chunk of chunk_tokens positions):
- * the KV head's pages are staged once in shared memory for all
- * q_heads/kv_heads query heads, scores use an online (running-max) softmax in
- * FP32 and chunks of one sequence are merged by the last CTA to finish.
+ * head_dim 128 with pages of 16-128 tokens runs on the tensor cores: one
+ * persistent CTA per SM, TMA page loads straight through the block table,
+ * S = K.Q^T and O = V^T.P^T on tcgen05 with FP32 accumulators in TMEM, so
+ * each page byte is read once for all q_heads/kv_heads query heads of its KV
+ * head.  The 128-token tiles of all (sequence, KV head) segments form one
+ * stream cut evenly across the CTAs (stream-K); a segment split between CTAs
+ * is merged from FP32 partials (m, l, O) by the last CTA to finish it, or,
+ * when few segments are cut into many pieces, by a separate merge kernel.
+ * head_dim 64 (and other page sizes) run a CUDA-core kernel: one CTA per
+ * (sequence, KV head, chunk of chunk_tokens positions), a cp.async ring and
+ * a warp-shuffle online softmax, chunks merged by the last CTA.
  * max_seq_len bounds seq_lens (it sizes the scratch); chunk_tokens 0 picks a
- * split from batch and max_seq_len.  seq_lens[b] == 0 yields zeros, like the
- * SDK's all-masked softmax.  Replaces decode_score_kernel,
- * decode_softmax_kernel and decode_attention_output_kernel
- * (attention_cuda.cu:343-398, launched :1001-1011). */
+ * split from batch and max_seq_len (the tensor-core kernel ignores it).
+ * seq_lens[b] == 0 yields zeros, like the SDK's all-masked softmax.
+ * Replaces decode_score_kernel, decode_softmax_kernel and
+ * decode_attention_output_kernel (attention_cuda.cu:343-398, launched
+ * :1001-1011). */
 int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch,
                      size_t q_heads, const void *query, float scale,
                      void *output, PkvDType output_dtype, size_t max_seq_len,
@@ -139,9 +147,13 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch,
  * behind an FFI that only passes the buffers it was given).  Shapes whose
  * scratch would exceed 8 MiB fail with an error naming the size.  Every GPU
  * that loads the library holds the 8 MiB until exit.  The first call on a
- * device looks up the array's device address (once per device), so make it
- * before any stream capture.  All calls share the array: calls that overlap
- * on the GPU (other streams, other threads) race; serialise them. */
+ * device looks up the array's device address (once per device, and again
+ * if the device's context changed, e.g. after cudaDeviceReset), so make it
+ * before any stream capture.  Arguments are checked before the array is
+ * touched: a refused call writes no device memory.  Each call clears the
+ * split-K tickets at the start of the array (one small memset on `stream`).
+ * All calls share the array: calls that overlap on the GPU (other streams,
+ * other threads) race; serialise them. */
 int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const PkvBatch *batch,
                                     size_t q_heads, const void *query, float scale,
                                     void *output, PkvDType output_dtype,

@@ -67,15 +67,23 @@ static size_t pages_for(size_t tokens, size_t page_tokens) {
     return tokens / page_tokens + (tokens % page_tokens != 0);
 }
 
+/* What a cache needs from its sizes: at least one token per page, one page
+ * and one sequence slot; page ids and slot numbers travel as 32-bit values
+ * (block tables, the low half of a handle); the token count of the whole
+ * pool and the two host arrays must be representable. */
+static int cache_sizes_valid(size_t block_size, size_t block_count, size_t max_sequences) {
+    if (block_size == 0 || block_count == 0 || max_sequences == 0) return 0;
+    const int ids_fit = block_count <= UINT32_MAX && max_sequences <= UINT32_MAX;
+    const int tokens_fit = block_count <= SIZE_MAX / block_size;
+    const int arrays_fit = block_count <= SIZE_MAX / sizeof(uint32_t) &&
+                           max_sequences <= SIZE_MAX / sizeof(SeqSlot);
+    return ids_fit && tokens_fit && arrays_fit;
+}
+
 int tensor_paged_kv_cache_create(size_t block_size, size_t block_count,
                                  size_t max_sequences,
                                  TensorPagedKVCache **cache) {
-    if (cache == NULL || block_size == 0 || block_count == 0 ||
-        max_sequences == 0 || block_count > UINT32_MAX ||
-        max_sequences > UINT32_MAX || block_count > SIZE_MAX / block_size ||
-        block_count > SIZE_MAX / sizeof(uint32_t) ||
-        max_sequences > SIZE_MAX / sizeof(SeqSlot))
-        return 0;
+    if (cache == NULL || !cache_sizes_valid(block_size, block_count, max_sequences)) return 0;
     *cache = NULL;
     TensorPagedKVCache *c = (TensorPagedKVCache *)calloc(1, sizeof(*c));
     if (c == NULL) return 0;
@@ -131,12 +139,17 @@ int tensor_paged_kv_sequence_create(TensorPagedKVCache *cache,
     return ok;
 }
 
-/* Caller holds the lock.  Makes room for `need` page ids in the slot. */
+/* Caller holds the lock.  Makes room for `need` page ids in the slot.  The
+ * vector grows by half its size (to at least `need` and at least 16 ids), so
+ * a sequence that gains a page per step reallocates a logarithmic number of
+ * times; the capacity is not observable through the API. */
 static int grow_pages(SeqSlot *s, size_t need) {
     if (need <= s->page_capacity) return 1;
-    size_t cap = s->page_capacity ? s->page_capacity : 4u;
-    while (cap < need) cap = cap > SIZE_MAX / 2u ? need : cap * 2u;
-    if (cap > SIZE_MAX / sizeof(uint32_t)) return 0;
+    if (need > SIZE_MAX / sizeof(uint32_t)) return 0;
+    size_t cap = s->page_capacity + s->page_capacity / 2u;
+    if (cap < need) cap = need;
+    if (cap < 16u) cap = 16u;
+    if (cap > SIZE_MAX / sizeof(uint32_t)) cap = need;
     uint32_t *p = (uint32_t *)realloc(s->pages, cap * sizeof(uint32_t));
     if (p == NULL) return 0;
     s->pages = p;

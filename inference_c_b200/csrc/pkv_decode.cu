@@ -1,21 +1,34 @@
 // pkv_decode.cu -- paged decode SDPA for sm_100a (one query token per sequence).
 //
-// Work unit = (sequence b, KV head g, chunk c of `chunk` positions).  A
-// persistent grid of 256-thread CTAs strides over the units.  Per unit:
-//   * the G = q_heads/kv_heads query heads of KV head g are held in registers
-//     (pre-scaled by scale*log2(e) so the softmax uses exp2);
-//   * 64-token tiles of K and V for head g are staged through a 3-deep
-//     cp.async ring straight from the pages named by the block table, so each
-//     page byte is read from HBM once for all G heads (GQA sharing);
-//   * QK: 16 lanes per token (one 16-byte chunk of the head row each), the G
-//     partial dots are reduce-scattered across the 16 lanes with shuffles;
-//   * running-max (online) softmax in FP32, one warp per query head;
-//   * PV: each thread owns one 16-byte column chunk and accumulates G x 8
-//     outputs in FP32 over its token group;
-//   * a unit covering a whole sequence writes the output directly; otherwise
-//     it writes (m, l, O) partials and the last unit of that (b, g) to finish
-//     (atomic ticket after __threadfence) merges all chunks.
-// The merge is the split-K combine of the SDK's Metal path
+// Two kernels behind pkv_paged_decode:
+//
+// paged_decode_tc_kernel (head_dim 128, pages of 16-128 tokens): tensor cores.
+//   One persistent 224-thread CTA per SM: a K producer warp and a V producer
+//   warp (TMA: the query rows of a GQA group and, per 128-token tile, every
+//   page of the tile straight from the pool through the block table, 128-byte
+//   swizzle), one thread issuing tcgen05.mma and a 4-warp softmax/merge group.
+//   Per tile:  S^T[128 tok][16] = K . Q^T  and  O^T[128 d][16] += V^T . P^T,
+//   FP32 accumulators in TMEM (M = tokens or dims, N = the query heads of the
+//   KV head padded to 16), so each page byte is read from HBM once for all
+//   its query heads.  P is written as a 16-bit high half plus the low
+//   remainder in the otherwise-zero rows of the N=16 operand (one MMA, ~22
+//   bits of P).  Work split is stream-K: the tiles of all (sequence, KV head)
+//   segments form one stream cut evenly across the CTAs; a segment cut
+//   between CTAs leaves FP32 partials (m, l, O) that the last CTA to finish
+//   it merges (atomic ticket), or, with few segments cut into many pieces,
+//   the separate pkv_tc_merge_kernel.
+//
+// paged_decode_simt_kernel (head_dim 64 or 128, any page size): CUDA cores.
+//   Work unit = (sequence b, KV head g, chunk c of `chunk` positions); a
+//   persistent grid of 256-thread CTAs strides over the units.  The G query
+//   heads of KV head g are held in registers (pre-scaled by scale*log2(e));
+//   64-token tiles of K and V stream through a 3-deep cp.async ring straight
+//   from the pages; 16 lanes per token for QK with shuffle reductions,
+//   running-max softmax in FP32, PV accumulated per 16-byte column chunk; a
+//   unit covering a whole sequence writes the output, otherwise it writes
+//   (m, l, O) partials and the last unit of (b, g) to finish merges them.
+//
+// The merges are the split-K combine of the SDK's Metal path
 // (attention_kernels.metal:693-875: per-partition max/sum/acc rescaled by
 // exp(m_i - m_max)); the result equals softmax(q.K^T * scale) . V as computed
 // by tensor_sdpa_f32 (attention.c:212-406) up to FP32 rounding.
@@ -1483,11 +1496,49 @@ constexpr size_t kDecodeStaticScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_decode_static_scratch[kDecodeStaticScratchBytes];
 
 std::mutex g_static_scratch_lock;
-void *g_static_scratch_addr[64];  // device address of the array, per device
+// Per device: the array's device address and the id of the CUDA context it
+// was looked up in.  The address belongs to that context; after a
+// cudaDeviceReset (or under another context) the module is loaded again,
+// possibly elsewhere, so a changed context id triggers a new lookup.
+struct StaticScratchSlot {
+    unsigned long long ctx_id;
+    void *addr;
+};
+StaticScratchSlot g_static_scratch[64];
 
-// The array's device address for the current device, looked up once per
-// device (with that device current).  In host code the symbol itself is only
-// a host-side stand-in and must never be handed to a kernel.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+// Unique id of the context current on this thread (0 when there is none or
+// the driver cannot say; 0 never matches a cached slot).
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static bool resolved = false;
+    if (!resolved) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+        resolved = true;
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS ||
+        ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// The array's device address for the current device, looked up with that
+// device current the first time a context of it calls (cudaGetSymbolAddress;
+// it allocates nothing).  In host code the symbol itself is only a host-side
+// stand-in and must never be handed to a kernel.
 void *static_scratch_for_current_device(char *error, size_t cap) {
     int dev = -1;
     cudaError_t st = cudaGetDevice(&dev);
@@ -1497,7 +1548,9 @@ void *static_scratch_for_current_device(char *error, size_t cap) {
         return nullptr;
     }
     std::lock_guard<std::mutex> guard(g_static_scratch_lock);
-    if (g_static_scratch_addr[dev] == nullptr) {
+    StaticScratchSlot &slot = g_static_scratch[dev];
+    const unsigned long long id = current_context_id();
+    if (slot.addr == nullptr || id == 0 || slot.ctx_id != id) {
         void *p = nullptr;
         st = cudaGetSymbolAddress(&p, g_decode_static_scratch);
         if (st != cudaSuccess || p == nullptr) {
@@ -1506,9 +1559,11 @@ void *static_scratch_for_current_device(char *error, size_t cap) {
                                    cudaGetErrorString(st));
             return nullptr;
         }
-        g_static_scratch_addr[dev] = p;
+        slot.addr = p;
+        // the lookup made the device's primary context current if none was
+        slot.ctx_id = id != 0 ? id : current_context_id();
     }
-    return g_static_scratch_addr[dev];
+    return slot.addr;
 }
 
 }  // namespace
@@ -1519,14 +1574,26 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
                                                size_t max_seq_len, PkvStream stream, char *error,
                                                size_t error_capacity) {
     const char *what = "pkv_paged_decode_static_scratch";
-    if (layer == nullptr || batch == nullptr || layer->kv_heads == 0) {
+    // Everything the scratch size depends on is checked before the array is
+    // touched, so a refused call writes no device memory.
+    if (layer == nullptr || batch == nullptr || query == nullptr || output == nullptr ||
+        layer->key_pool == nullptr || layer->value_pool == nullptr ||
+        batch->block_tables == nullptr || batch->seq_lens == nullptr) {
         pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    const size_t kvh = layer->kv_heads, hd = layer->head_dim;
+    if (batch->batch == 0 || batch->batch > (size_t)pkv::kMaxBatch || kvh == 0 ||
+        q_heads == 0 || q_heads % kvh != 0 || q_heads > 65536 || (hd != 64 && hd != 128) ||
+        max_seq_len > INT32_MAX / 2) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: invalid batch (1..%d), heads, head_dim or max_seq_len", what,
+                               pkv::kMaxBatch);
         return 0;
     }
     // Scratch of the kernel pkv_paged_decode will pick for this shape;
     // anything above the array is refused.
-    const size_t kvh = layer->kv_heads, hd = layer->head_dim;
-    const size_t group = q_heads % kvh == 0 ? q_heads / kvh : 0;
+    const size_t group = q_heads / kvh;
     size_t need;
     if (pkv::tc_eligible(hd, layer->block_size, group, layer->block_count * layer->block_size)) {
         need = pkv::tc_workspace(batch->batch, kvh).total;
@@ -1543,8 +1610,12 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
     }
     void *scratch = static_scratch_for_current_device(error, error_capacity);
     if (scratch == nullptr) return 0;
-    // The split-K tickets must start at zero; both layouts keep them first.
-    const size_t tickets = pkv::round_up(batch->batch * layer->kv_heads * sizeof(uint32_t), 256);
+    // The split-K tickets must be zero when a decode starts; both layouts
+    // keep them first.  A decode that completes leaves them at zero, but one
+    // that gave up part-way (a bounded wait that expired) may not, and the
+    // array outlives every call, so each call clears them (one small memset
+    // on the caller's stream).
+    const size_t tickets = pkv::round_up(batch->batch * kvh * sizeof(uint32_t), 256);
     const cudaError_t st = cudaMemsetAsync(scratch, 0, tickets, (cudaStream_t)stream);
     if (st != cudaSuccess) {
         pkv_internal_set_error(error, error_capacity, "%s: clearing the tickets failed: %s", what,

@@ -108,7 +108,13 @@ HostStage g_stage;
 bool stage_ready(int dev) {
     if (g_stage.buf[0] != nullptr && g_stage.device == dev) return true;
     for (int i = 0; i < 2; ++i) {
-        if (g_stage.done[i] != nullptr) cudaEventDestroy(g_stage.done[i]);
+        // An earlier call that failed part-way may have left a copy from
+        // this pinned buffer in flight on the old device: wait for it before
+        // the buffer is refilled under new events.
+        if (g_stage.done[i] != nullptr) {
+            cudaEventSynchronize(g_stage.done[i]);
+            cudaEventDestroy(g_stage.done[i]);
+        }
         g_stage.done[i] = nullptr;
         if (g_stage.buf[i] == nullptr &&
             cudaHostAlloc(reinterpret_cast<void **>(&g_stage.buf[i]), kStageChunk,
@@ -322,7 +328,14 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
     if (!pkv_sdpa_f16(dq, dk, dv, mb != 0 ? dm : nullptr, dout, batch, query_heads, kv_heads,
                       query_length, kv_length, scale, causal, dws, wsb, nullptr, nullptr, 0))
         return 0;
-    return stage_download(output, dout, qb, k) && cudaStreamSynchronize(nullptr) == cudaSuccess;
+    if (!stage_download(output, dout, qb, k) || cudaStreamSynchronize(nullptr) != cudaSuccess)
+        return 0;
+    // The kernel never traps: a bounded wait that gave up or an addressing
+    // fault leaves a code in the prefill fault word and the output partial.
+    // Only that word is read (and cleared) here, so fault codes of the other
+    // kernels stay for pkv_device_fault.
+    uint32_t fault = 0;
+    return pkv_internal_take_prefill_fault(&fault) && fault == 0;
 }
 
 }  // extern "C"

@@ -44,6 +44,12 @@ int pkv_internal_take_decode_fault(uint32_t *code);
 int pkv_internal_take_prefill_fault(uint32_t *code);
 int pkv_internal_take_sequence_fault(uint32_t *code);
 
+/* Writes `code` into the prefill fault word of the current device: a
+ * host-side stand-in for a kernel that recorded a fault, so tests can check
+ * that callers report it (no kernel runs, nothing faults).  Exported for the
+ * tests only. */
+int pkv_internal_plant_prefill_fault(uint32_t code);
+
 /* pkv_paged_prefill with the general options the dense SDPA needs: an
  * additive FP16 mask [query row of the chunk][key] with a row stride in
  * elements (NULL: none), dense mode (a chunk may be longer than its

@@ -914,4 +914,8 @@ int pkv_internal_take_prefill_fault(uint32_t *code) {
     return cudaMemcpyToSymbol(pkv::g_prefill_fault, &zero, sizeof(uint32_t)) == cudaSuccess;
 }
 
+int pkv_internal_plant_prefill_fault(uint32_t code) {
+    return cudaMemcpyToSymbol(pkv::g_prefill_fault, &code, sizeof(uint32_t)) == cudaSuccess;
+}
+
 }  // extern "C"

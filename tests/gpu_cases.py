@@ -88,3 +88,59 @@ class PagedCase:
     def batch(self):
         from inference_c_b200 import make_batch
         return make_batch(self.d_tables, self.d_lens)
+
+
+def host_threads() -> int:
+    import os
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # pragma: no cover
+        return max(1, os.cpu_count() or 1)
+
+
+def sdk_paged_attention(oracle_mod, dtype: str, q: np.ndarray, q_offsets, kpool: np.ndarray,
+                        vpool: np.ndarray, kv_heads: int, head_dim: int, block_size: int,
+                        tables: np.ndarray, seq_lens: np.ndarray, q_heads: int, scale: float,
+                        causal: bool) -> list[np.ndarray]:
+    """Attention of every sequence of a paged batch, on all host threads:
+    the SDK's own tensor_sdpa_f32 (oracle/_ref, through RefJob) where it was
+    built, else the CPU restatement (which matches it bit for bit).  q holds
+    storage bits, [rows][q_heads][head_dim]; q_offsets (None: one row per
+    sequence) gives each sequence's rows, its last positions.  Returns one
+    float32 [rows_b][q_heads][head_dim] array per sequence."""
+    from concurrent.futures import ThreadPoolExecutor
+    n = len(seq_lens)
+    offs = np.arange(n + 1) if q_offsets is None else np.asarray(q_offsets, np.int64)
+    if oracle_mod.ref_available():
+        job = oracle_mod.RefJob(dtype, q, None if q_offsets is None else offs.astype(np.int32),
+                                kpool, vpool, kv_heads, head_dim, block_size, tables, seq_lens,
+                                q_heads, scale, causal)
+        try:
+            job.run(host_threads())
+            return [job.output(i) for i in range(n)]
+        finally:
+            job.close()
+
+    def one(b):
+        L = int(seq_lens[b])
+        rows = np.arange(offs[b], offs[b + 1])
+        pos = L - len(rows) + np.arange(len(rows))
+        return oracle_mod.paged_attention_rows(q[rows], pos, causal, dtype, kpool, vpool,
+                                               kv_heads, head_dim, block_size, tables[b], L,
+                                               scale)
+
+    with ThreadPoolExecutor(host_threads()) as ex:  # the ctypes calls release the GIL
+        return list(ex.map(one, range(n)))
+
+
+def report(what: str, max_abs: float, max_rel: float) -> None:
+    """Prints a full-size parity result beside the tolerances (shown by
+    pytest -rP) and appends it to the file PKV_PARITY_LOG names, if set."""
+    import os
+    line = (f"PARITY {what}: max-abs {max_abs:.3e} (tol {ABS_TOL}), "
+            f"max-rel {max_rel:.3e} over |ref| >= {REL_FLOOR} (tol {REL_TOL})")
+    print(line)
+    log = os.environ.get("PKV_PARITY_LOG")  # optional: collect the lines of a run
+    if log:
+        with open(log, "a") as f:
+            f.write(line + "\n")

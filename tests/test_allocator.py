@@ -126,6 +126,19 @@ def test_sdk_unit_test_binary_against_our_allocator():
     assert "allocator tests passed" in out.stdout
 
 
+def test_sdk_decoder_test_binary_links_and_runs_on_cpu():
+    """The SDK's tests/test_attention.c built unchanged against
+    libpkv_b200.so (oracle/Makefile) loads this library, and its CPU part
+    (the tensor_sdpa_f32 known answers) passes; without a GPU its decoder
+    cases report themselves skipped (the GPU test runs them)."""
+    exe = ROOT / "oracle" / "_ref" / "test_attention_ours"
+    if not exe.exists():
+        pytest.skip("needs the SDK's test source (built by oracle/Makefile)")
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert "attention tests passed" in out.stdout
+
+
 def test_threads_never_double_allocate(lib):
     """Concurrent reserve/release from 8 threads: every page is owned by at
     most one sequence and all pages come back."""

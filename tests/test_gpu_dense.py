@@ -71,6 +71,25 @@ def test_host_hook_and_sdk_cpu(lib, oracle_mod, cuda):
         check_close(got, want, "host hook vs SDK tensor_sdpa_f32")
 
 
+def test_host_hook_reports_a_recorded_fault(lib, oracle_mod, cuda):
+    """A fault code left in the prefill kernel's fault word makes the run_f16
+    hook return 0 (its output would be partial).  The code is planted from
+    the host -- no kernel faults -- and the hook clears it: the next call
+    succeeds and matches the oracle."""
+    import ctypes
+    q, k, v = case(1, 4, 2, 32, 64, seed=3)
+    plant = lib.pkv_internal_plant_prefill_fault
+    plant.argtypes, plant.restype = [ctypes.c_uint32], ctypes.c_int
+    assert plant(4) == 1
+    bits = (q.view(np.uint16), k.view(np.uint16), v.view(np.uint16))
+    assert P.sdpa_f16_host(*bits, 0.1, True) is None
+    got = P.sdpa_f16_host(*bits, 0.1, True)
+    assert got is not None
+    check_close(got.view(np.float16).astype(np.float32), expected(q, k, v, 0.1, True, oracle_mod),
+                "host hook after a reported fault")
+    assert P.device_fault(0) == 0
+
+
 def make_mask(Lq, Lk, seed, dead_rows=()):
     """N(0, 2) additive mask with ~10 % -inf entries and fully masked rows."""
     rng = np.random.default_rng(seed)

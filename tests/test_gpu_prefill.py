@@ -1,7 +1,9 @@
 """GPU parity of pkv_paged_prefill (tcgen05 chunked prefill over the paged
 cache) against the oracle -- the SDK's tensor_sdpa_f32 semantics with the
 causal offset kv_len - q_len -- within max-abs 2e-3 / max-rel 1e-2; at config
-5's full size through sampled rows and an exact V-scaling property."""
+5's full size through one whole sequence against the SDK's own
+tensor_sdpa_f32, sampled rows of the others and an exact V-scaling
+property."""
 from __future__ import annotations
 
 import base64
@@ -13,7 +15,7 @@ import pytest
 
 import inference_c_b200 as P
 from inference_c_b200 import workloads as W
-from tests.gpu_cases import check_close, to_device_bits, to_host_bits
+from tests.gpu_cases import check_close, report, sdk_paged_attention, to_device_bits, to_host_bits
 
 pytestmark = pytest.mark.gpu
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
@@ -113,21 +115,40 @@ def test_prefill_storage_dtype_output(lib, oracle_mod, cuda):
 
 def test_cfg5_full_size(lib, oracle_mod, cuda):
     """Config 5 at full size: 8 sequences of 8192 past + 2048 new BF16 tokens,
-    GQA 32/8, causal within the chunk.  Sampled rows (chunk start, tile
-    edges, end) of two sequences against the oracle; doubling V doubles every
-    output exactly."""
+    GQA 32/8, causal within the chunk.  One whole sequence (all 2048 chunk
+    rows x 32 heads) against the SDK's tensor_sdpa_f32 on all host threads,
+    sampled rows (chunk start, tile edges, end) of the other seven against
+    the oracle; doubling V doubles every output exactly."""
     import torch
     c = W.CONFIGS[5]
     case = PrefillCase([W.CFG5_PAST] * 8, [W.CFG5_CHUNK] * 8, c.q_heads, c.kv_heads, "bf16",
                        seed=5, device=cuda)
     got = case.run(True)
     assert np.isfinite(got).all()
+    # sequence 3 in full: its chunk cut into 16 blocks of 128 rows, block j a
+    # "sequence" of length past + 128(j + 1) with the same pages (the causal
+    # offset kv_len - q_len then places its rows exactly), so the host
+    # threads share the work
+    b, blk = 3, 128
+    nb = W.CFG5_CHUNK // blk
+    r0 = int(case.offs[b])
+    q_rows = np.ascontiguousarray(case.q[r0:r0 + W.CFG5_CHUNK])
+    lens = W.CFG5_PAST + blk * np.arange(1, nb + 1)
+    tabs = np.repeat(case.tables[b:b + 1], nb, axis=0)
+    outs = sdk_paged_attention(oracle_mod, "bf16", q_rows, blk * np.arange(nb + 1), case.kpool,
+                               case.vpool, c.kv_heads, 128, 16, tabs, lens, c.q_heads,
+                               float(1 / np.sqrt(128)), True)
+    whole = np.concatenate(outs)
+    report("cfg5 sequence 3, all 2048 rows x 32 heads, vs SDK tensor_sdpa_f32",
+           *check_close(got[r0:r0 + W.CFG5_CHUNK], whole, "cfg5 whole sequence"))
     rows = []
-    for b in (0, 7):
-        base = int(case.offs[b])
-        rows += [base + r for r in (0, 1, 127, 128, 1023, 1919, 2046, 2047)]
+    for s in range(8):
+        if s != b:
+            base = int(case.offs[s])
+            rows += [base + r for r in (0, 1, 127, 128, 1023, 1919, 2046, 2047)]
     want = case.oracle(oracle_mod, True, rows)
-    check_close(got[rows], want[rows], "cfg5 sampled rows")
+    report("cfg5 sampled rows of the other 7 sequences",
+           *check_close(got[rows], want[rows], "cfg5 sampled rows"))
     case.d_v.mul_(2)
     twice = case.run(True)
     assert np.array_equal(twice, 2 * got)

@@ -206,3 +206,21 @@ def test_fast_attention_paths_and_pages(oracle_mod, hd, qh, kvh):
         assert_tokens_agree(got, ref, logits, "SDK CUDA backend")
     assert P.device_fault(0) == 0
     cache.free()
+
+
+def test_sdk_decoder_test_binary_unchanged():
+    """The SDK's own tests/test_attention.c, compiled unchanged by
+    oracle/Makefile with libpkv_b200.so providing the paged entry point and
+    the allocator (the SDK's CUDA backend provides the contiguous decoders).
+    Its paged-vs-contiguous token memcmp cases (F16 decode split over two
+    calls, host prefix import with a rejected call first, a 1025-token
+    prefix, two interleaved sequences, F32 storage, Q8_0 and Q4_0 weights)
+    must run -- none may report itself skipped -- and pass."""
+    import subprocess
+    exe = O.HERE / "_ref" / "test_attention_ours"
+    if not exe.exists():
+        pytest.skip("needs the SDK's test source (built by oracle/Makefile)")
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "attention tests passed" in out.stdout
+    assert "skipped" not in out.stdout, out.stdout

@@ -179,3 +179,31 @@ def test_port_equals_sdk_live(oracle_mod, group, dtype, causal):
             assert np.max(np.abs(got - want)) <= 1e-6
         else:
             assert np.array_equal(got, want)
+
+
+def test_threaded_sdk_reference_splits_a_causal_chunk_exactly(oracle_mod):
+    """The full-size GPU tests cut a causal chunk into row blocks, block j a
+    sequence of length past + its last row, so the host threads share the
+    SDK's tensor_sdpa_f32 calls; that must give the same bits as the
+    restatement on the whole chunk, and the decode form (one row per
+    sequence) the same as paged_decode."""
+    from tests.gpu_cases import sdk_paged_attention
+    lengths = np.array([300 + 64], np.int64)
+    tables, _ = W.shuffled_tables(lengths, 16, 40, seed=4)
+    kp = W.normal_bits(4, (40 * 16, 2 * 64), "bf16", stream=1)
+    vp = W.normal_bits(4, (40 * 16, 2 * 64), "bf16", stream=2)
+    q = W.normal_bits(4, (64, 8, 64), "bf16", stream=3)
+    whole = oracle_mod.paged_attention_rows(q, 300 + np.arange(64), True, "bf16", kp, vp, 2, 64,
+                                            16, tables[0], 364, 0.125)
+    blk = 16
+    outs = sdk_paged_attention(oracle_mod, "bf16", q, blk * np.arange(5), kp, vp, 2, 64, 16,
+                               np.repeat(tables, 4, axis=0), 300 + blk * np.arange(1, 5), 8,
+                               0.125, True)
+    assert np.array_equal(np.concatenate(outs), whole)
+    lens = np.array([5, 200, 17], np.int64)
+    t3, _ = W.shuffled_tables(lens, 16, 40, seed=5)
+    q3 = W.normal_bits(5, (3, 8, 64), "bf16", stream=3)
+    dec = sdk_paged_attention(oracle_mod, "bf16", q3, None, kp, vp, 2, 64, 16, t3, lens, 8,
+                              0.125, False)
+    want = oracle_mod.paged_decode(q3, "bf16", kp, vp, 2, 64, 16, t3, lens, 0.125)
+    assert np.array_equal(np.stack([o[0] for o in dec]), want)
