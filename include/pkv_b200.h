@@ -161,8 +161,9 @@ int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const PkvBatch *
                                     size_t error_capacity);
 
 /* Chunked prefill over the paged cache (tcgen05 tensor cores, FP32
- * accumulation in TMEM).  Sequence b contributes query rows
- * query_offsets[b] .. query_offsets[b+1]-1 ([total_q][q_heads][head_dim]);
+ * accumulation in TMEM; head_dim 64 or 128, pages of 16-128 tokens).
+ * Sequence b contributes query rows query_offsets[b] ..
+ * query_offsets[b+1]-1 ([total_q][q_heads][head_dim]);
  * they are its LAST n_b positions, so query j sees keys
  * 0 .. seq_lens[b]-n_b+j when causal (the SDK's causal offset
  * kv_len - q_len, attention.c:251,352) and all seq_lens[b] keys otherwise.
@@ -189,26 +190,32 @@ int pkv_device_fault(int device, uint32_t *code, char *error,
 int pkv_selftest_wait_timeout(uint32_t *code, char *error, size_t error_capacity);
 
 /* Dense FP16 SDPA on the tcgen05 prefill kernel: query [batch][q_heads]
- * [q_len][128], key/value [batch][kv_heads][kv_len][128], output like query,
- * optional additive mask [q_len][kv_len] (NULL: none; shared by every batch
- * and head), all device pointers (tensors 16-byte aligned, the mask 2-byte).
- * GQA (q_heads a multiple of kv_heads), score = q.k * scale + mask, causal
- * rule key > query + max(kv_len - q_len, 0), FP32 accumulation, FP16 output;
+ * [q_len][head_dim], key/value [batch][kv_heads][kv_len][head_dim], output
+ * like query, optional additive mask [q_len][kv_len] (NULL: none; shared by
+ * every batch and head), all device pointers (tensors 16-byte aligned, the
+ * mask 2-byte).  head_dim 64 or 128 (value_dim = head_dim).  GQA (q_heads a
+ * multiple of kv_heads), score = q.k * scale + mask, causal rule
+ * key > query + max(kv_len - q_len, 0), FP32 accumulation, FP16 output;
  * a row whose maximum score is not finite (all keys -inf, or a +inf) is
  * zero.  Replaces the CUDA backend's dense sdpa<T> (attention_cuda.cu:25-99)
  * behind tensor_sdpa_f16 (attention.c:408-459).  Each (batch, KV head) is
  * one sequence of the paged prefill kernel with an identity page table. */
 size_t pkv_sdpa_workspace_bytes(size_t batch, size_t q_heads, size_t kv_heads,
-                                size_t q_len, size_t kv_len);
+                                size_t q_len, size_t kv_len, size_t head_dim);
 int pkv_sdpa_f16(const void *query, const void *key, const void *value,
                  const void *additive_mask, void *output, size_t batch,
                  size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
-                 float scale, int causal, void *workspace, size_t workspace_bytes,
-                 PkvStream stream, char *error, size_t error_capacity);
+                 size_t head_dim, float scale, int causal, void *workspace,
+                 size_t workspace_bytes, PkvStream stream, char *error,
+                 size_t error_capacity);
 /* The same with host tensors, in the argument order of the SDK backend hook
  * run_f16 (src/attention_backend.h:14-18), so it can be installed as that
  * hook: uploads, computes on the current device, downloads, synchronous.
- * Returns 0 for head_dim/value_dim other than 128.  Its first call allocates,
+ * Takes head_dim = value_dim = 64 or 128; returns 0 for other shapes (the
+ * SDK's sdpa<T> also allows value_dim != head_dim and any head_dim; those
+ * calls are refused here, not computed another way).  Returns 0 as well
+ * when the kernel recorded a fault (its prefill fault word is read and
+ * cleared after the call).  Its first call allocates,
  * and keeps until exit, a device buffer sized for the largest call so far
  * and 32 MiB of pinned host memory (two staging buffers that up to 8 host
  * threads fill while the DMA engine moves the other); calls are serialised

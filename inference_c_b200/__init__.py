@@ -145,8 +145,8 @@ EXPORTS = {
     "pkv_selftest_wait_timeout": (_c_int, [ctypes.POINTER(ctypes.c_uint32), *_ERR]),
     "pkv_sdpa_workspace_bytes": (_c_size, [_c_size, _c_size, _c_size, _c_size, _c_size]),
     "pkv_sdpa_f16": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size, _c_size,
-                              _c_size, _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size, _c_ptr,
-                              *_ERR]),
+                              _c_size, _c_size, _c_size, ctypes.c_float, _c_int, _c_ptr, _c_size,
+                              _c_ptr, *_ERR]),
     "pkv_sdpa_f16_host": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_size,
                                    _c_size, _c_size, _c_size, _c_size, _c_size, ctypes.c_float,
                                    _c_int]),
@@ -507,15 +507,15 @@ def decode_cache_clear() -> None:
 
 def sdpa_f16(query, key, value, output, scale: float, causal: bool, stream=None,
              mask=None) -> None:
-    """query/output [B, Hq, Lq, 128], key/value [B, Hkv, Lk, 128] float16 CUDA tensors;
-    mask: None or an additive float16 CUDA tensor [Lq, Lk]."""
+    """query/output [B, Hq, Lq, d], key/value [B, Hkv, Lk, d] float16 CUDA tensors
+    (d = 64 or 128); mask: None or an additive float16 CUDA tensor [Lq, Lk]."""
     import torch
     B, Hq, Lq, d = query.shape
     Hkv, Lk = key.shape[1], key.shape[2]
-    n = load().pkv_sdpa_workspace_bytes(B, Hq, Hkv, Lq, Lk)
+    n = load().pkv_sdpa_workspace_bytes(B, Hq, Hkv, Lq, Lk, d)
     ws = torch.empty(n, dtype=torch.uint8, device=query.device)
     _call("pkv_sdpa_f16", query.data_ptr(), key.data_ptr(), value.data_ptr(),
-          None if mask is None else mask.data_ptr(), output.data_ptr(), B, Hq, Hkv, Lq, Lk,
+          None if mask is None else mask.data_ptr(), output.data_ptr(), B, Hq, Hkv, Lq, Lk, d,
           ctypes.c_float(scale), int(causal), ws.data_ptr(), n, _stream_ptr(stream))
 
 

@@ -5,20 +5,20 @@
 // src/attention_backend.h; the CUDA backend's sdpa<T>, attention_cuda.cu:
 // 25-99, materialises every score row).  Here each (batch, KV head) becomes
 // one "sequence" of the paged prefill kernel with an identity page table:
-//   * K and V of (b, g) are kv_len contiguous rows of 128 elements, i.e. a
+//   * K and V of (b, g) are kv_len contiguous rows of head_dim elements, i.e. a
 //     pool with one KV head whose pages are consecutive; when kv_len is a
 //     multiple of 16 the tensors themselves are the pool (no copy), otherwise
 //     each sequence is copied to a whole number of 16-row pages;
 //   * the query and output tensors are read and written in place: the
 //     kernel's dense layout addresses head (b, h) row i at ((b*Hq + h)*Lq +
-//     i)*128, the group of KV head g being heads g*G .. g*G+G-1;
+//     i)*head_dim, the group of KV head g being heads g*G .. g*G+G-1;
 //   * the causal rule key > query + max(kv_len - q_len, 0) is the prefill
 //     kernel's own (in dense mode, which lets q_len exceed kv_len);
 //   * an additive FP16 mask [q_len][kv_len] (shared by every batch and head,
 //     as the SDK's) is added to the scaled scores inside the kernel's softmax;
 //     a row whose maximum is not finite gives zeros (the CUDA backend's rule,
 //     softmax_rows_kernel, attention_cuda.cu:45-55).
-// head_dim = value_dim = 128.
+// head_dim = value_dim, 64 or 128 (the prefill kernel's instantiations).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -34,20 +34,22 @@
 namespace pkv {
 namespace {
 
-constexpr int kDHead = 128;
 constexpr int kPage = 16;
-constexpr int kChunks = kDHead / 8;  // 16-byte chunks per row
 
-// K or V of every (b, g) into a whole number of 16-row pages.
-__global__ void pad_rows_kernel(const uint4 *src, uint4 *dst, int64_t S, int Lk, int pages) {
-    const int64_t n = S * (int64_t)Lk * kChunks;
+bool head_dim_ok(size_t d) { return d == 64 || d == 128; }
+
+// K or V of every (b, g) into a whole number of 16-row pages; `chunks` is
+// the number of 16-byte chunks in a row (head_dim / 8).
+__global__ void pad_rows_kernel(const uint4 *src, uint4 *dst, int64_t S, int Lk, int pages,
+                                int chunks) {
+    const int64_t n = S * (int64_t)Lk * chunks;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
          e += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(e % kChunks);
-        const int64_t r = e / kChunks;
+        const int c = (int)(e % chunks);
+        const int64_t r = e / chunks;
         const int64_t s = r / Lk;
         const int i = (int)(r - s * Lk);
-        dst[((s * pages * kPage) + i) * kChunks + c] = src[e];
+        dst[((s * pages * kPage) + i) * chunks + c] = src[e];
     }
 }
 
@@ -70,7 +72,7 @@ struct DenseLayout {
     size_t tables, lens, offs, kpad, vpad, total;
 };
 
-DenseLayout dense_layout(size_t B, size_t Hq, size_t Hkv, size_t Lq, size_t Lk) {
+DenseLayout dense_layout(size_t B, size_t Hq, size_t Hkv, size_t Lq, size_t Lk, size_t d) {
     const size_t S = B * Hkv, pages = (Lk + kPage - 1) / kPage;
     const bool pad = Lk % kPage != 0;
     DenseLayout w;
@@ -78,8 +80,8 @@ DenseLayout dense_layout(size_t B, size_t Hq, size_t Hkv, size_t Lq, size_t Lk) 
     w.lens = w.tables + align256(S * pages * 4);
     w.offs = w.lens + align256(S * 4);
     w.kpad = w.offs + align256((S + 1) * 4);
-    w.vpad = w.kpad + (pad ? align256(S * pages * kPage * kDHead * 2) : 0);
-    w.total = w.vpad + (pad ? align256(S * pages * kPage * kDHead * 2) : 0);
+    w.vpad = w.kpad + (pad ? align256(S * pages * kPage * d * 2) : 0);
+    w.total = w.vpad + (pad ? align256(S * pages * kPage * d * 2) : 0);
     return w;
 }
 
@@ -207,15 +209,15 @@ bool stage_download(void *dst, const void *src, size_t n, unsigned &k) {
 extern "C" {
 
 size_t pkv_sdpa_workspace_bytes(size_t batch, size_t q_heads, size_t kv_heads, size_t q_len,
-                                size_t kv_len) {
-    return pkv::dense_layout(batch, q_heads, kv_heads, q_len, kv_len).total;
+                                size_t kv_len, size_t head_dim) {
+    return pkv::dense_layout(batch, q_heads, kv_heads, q_len, kv_len, head_dim).total;
 }
 
 int pkv_sdpa_f16(const void *query, const void *key, const void *value,
                  const void *additive_mask, void *output, size_t batch, size_t q_heads,
-                 size_t kv_heads, size_t q_len, size_t kv_len, float scale, int causal,
-                 void *workspace, size_t workspace_bytes, PkvStream stream, char *error,
-                 size_t error_capacity) {
+                 size_t kv_heads, size_t q_len, size_t kv_len, size_t head_dim, float scale,
+                 int causal, void *workspace, size_t workspace_bytes, PkvStream stream,
+                 char *error, size_t error_capacity) {
     using namespace pkv;
     const char *what = "pkv_sdpa_f16";
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
@@ -227,14 +229,14 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
         q_heads % kv_heads != 0 || q_heads / kv_heads > 65535 || q_len > (1u << 30) ||
         kv_len > (1u << 30) || batch * kv_heads > (1u << 24) ||
         batch * q_heads * q_len >= (size_t(1) << 31) || (causal != 0 && causal != 1) ||
-        !isfinite(scale)) {
+        !isfinite(scale) || !head_dim_ok(head_dim)) {
         pkv_internal_set_error(error, error_capacity,
-                               "%s: needs q_heads a multiple of kv_heads, a finite scale and "
-                               "causal 0 or 1",
+                               "%s: needs head_dim 64 or 128, q_heads a multiple of kv_heads, a "
+                               "finite scale and causal 0 or 1",
                                what);
         return 0;
     }
-    const DenseLayout w = dense_layout(batch, q_heads, kv_heads, q_len, kv_len);
+    const DenseLayout w = dense_layout(batch, q_heads, kv_heads, q_len, kv_len, head_dim);
     if (workspace_bytes < w.total || (uintptr_t)workspace % 256 ||
         ((uintptr_t)query | (uintptr_t)key | (uintptr_t)value | (uintptr_t)output) % 16) {
         pkv_internal_set_error(error, error_capacity,
@@ -255,13 +257,14 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
     tables_kernel<<<grid_for(S * pages + S + 1), 256, 0, s>>>(tables, lens, offs, S, pages,
                                                               (int)kv_len, (int)q_len);
     if (pad) {
-        const int64_t kn = S * (int64_t)kv_len * kChunks;
+        const int chunks = (int)(head_dim / 8);
+        const int64_t kn = S * (int64_t)kv_len * chunks;
         pad_rows_kernel<<<grid_for(kn), 256, 0, s>>>(static_cast<const uint4 *>(key),
                                                       reinterpret_cast<uint4 *>(ws + w.kpad), S,
-                                                      (int)kv_len, pages);
+                                                      (int)kv_len, pages, chunks);
         pad_rows_kernel<<<grid_for(kn), 256, 0, s>>>(static_cast<const uint4 *>(value),
                                                       reinterpret_cast<uint4 *>(ws + w.vpad), S,
-                                                      (int)kv_len, pages);
+                                                      (int)kv_len, pages, chunks);
         kpool = ws + w.kpad;
         vpool = ws + w.vpad;
     }
@@ -275,7 +278,7 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
     layer.block_size = kPage;
     layer.block_count = (size_t)S * pages;
     layer.kv_heads = 1;
-    layer.head_dim = kDHead;
+    layer.head_dim = head_dim;
     layer.dtype = PKV_DTYPE_F16;
     PkvBatch b;
     b.block_tables = tables;
@@ -296,16 +299,16 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
                       int causal) {
     using namespace pkv;
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
-        head_dim != kDHead || value_dim != kDHead || batch == 0 || query_heads == 0 ||
+        !head_dim_ok(head_dim) || value_dim != head_dim || batch == 0 || query_heads == 0 ||
         kv_heads == 0 || query_length == 0 || kv_length == 0 || query_heads % kv_heads != 0)
         return 0;
     std::lock_guard<std::mutex> lock(g_host_mutex);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-    const size_t qb = batch * query_heads * query_length * kDHead * 2;
-    const size_t kb = batch * kv_heads * kv_length * kDHead * 2;
+    const size_t qb = batch * query_heads * query_length * head_dim * 2;
+    const size_t kb = batch * kv_heads * kv_length * head_dim * 2;
     const size_t wsb = pkv_sdpa_workspace_bytes(batch, query_heads, kv_heads, query_length,
-                                                kv_length);
+                                                kv_length, head_dim);
     const size_t mb = additive_mask != nullptr ? query_length * kv_length * 2 : 0;
     const size_t need = align256(qb) * 2 + align256(kb) * 2 + align256(mb) + wsb;
     if (g_host_ws_bytes[dev] < need) {
@@ -326,7 +329,8 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
         (mb != 0 && !stage_upload(dm, additive_mask, mb, k)))
         return 0;
     if (!pkv_sdpa_f16(dq, dk, dv, mb != 0 ? dm : nullptr, dout, batch, query_heads, kv_heads,
-                      query_length, kv_length, scale, causal, dws, wsb, nullptr, nullptr, 0))
+                      query_length, kv_length, head_dim, scale, causal, dws, wsb, nullptr,
+                      nullptr, 0))
         return 0;
     if (!stage_download(output, dout, qb, k) || cudaStreamSynchronize(nullptr) != cudaSuccess)
         return 0;

@@ -8,27 +8,30 @@
 // Work item = 128 query rows of two query heads of the same KV head (one head
 // when the GQA group is odd).  One persistent 384-thread CTA per SM:
 //   warp 0       producer: TMA-loads the item's query rows of both heads
-//                (3-D boxes over [rows][heads][128]) and, per 128-key tile,
-//                every page of K and V of the KV head straight from the pool
-//                (2-D boxes of one page x 64 columns); K and V rings of 2;
+//                (3-D boxes over [rows][heads][head_dim]) and, per 128-key
+//                tile, every page of K and V of the KV head straight from the
+//                pool (2-D boxes of one page x 64 columns); K and V rings of 2;
 //   warp 1       one thread issues tcgen05.mma, interleaving the two heads
 //                so each softmax group works while the tensor cores serve
 //                the other:  S_A(j), PV_B(j-1), S_B(j), PV_A(j), ...
-//                  S[128 q][128 k]  = Q[128][128] . K^T          (smem x smem)
-//                  O[128 q][128 d] += P[128 q][128 k] . V[128][128] (P in TMEM)
+//                  S[128 q][128 k] = Q[128][d] . K^T          (smem x smem)
+//                  O[128 q][d]    += P[128 q][128 k] . V[128][d] (P in TMEM)
 //   warps 4-7    softmax of head A, warps 8-11 softmax of head B: thread r
 //                owns query row r (TMEM lane r), so row max and sum need no
-//                cross-thread traffic.  Two passes over S in TMEM (max, then
-//                exp) keep 32 scores in registers at a time.
+//                cross-thread traffic; all 128 scores of a row come from one
+//                TMEM load.
 // Each head's P replaces its S in TMEM as 16-bit pairs, a high half and a
 // low half (p - round(p)) per 32-key chunk, and feeds the PV MMA as the
-// A operand (two MMAs: high then low); with P rounded to bf16 alone the
-// output error (~1e-4 at 2k-10k keys) passes max-abs 2e-3 but its tail
-// breaks max-rel 1e-2 on outputs near 1e-2, so the split is always on.
+// A operand (two MMAs: high then low, ~22 bits of P).  One 16-bit P alone is
+// not enough: with BF16 P the output error (~1e-4 at 2k-10k keys) breaks
+// max-rel 1e-2 on outputs near 1e-2, and with FP16 P (V converted to FP16)
+// rows over a few keys whose terms cancel reach 1.1e-2 (measured on the
+// golden small case), so the split is always on.
 // O accumulates in TMEM (FP32); the running max is raised only when a tile's
 // max exceeds it by more than 2^8 (lazy rescale of O in TMEM).  A head's S/P
 // buffer is reused for its next tile only after its PV completed.  TMEM:
-// head A S/P 0-127, O 128-255; head B S/P 256-383, O 384-511.
+// head A S/P 0-127, O 128-(128+d); head B S/P 256-383, O 384-(384+d).
+// head_dim d is 64 or 128 (one or two 64-column halves per row).
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <stdio.h>
@@ -276,9 +279,9 @@ __device__ __forceinline__ void store_row32(OT *dst, const uint32_t (&v)[32], fl
     }
 }
 
-// S[128 q][128 k] = Q . K^T: eight K=16 steps over the two 64-column halves
-// of Q and K (SWIZZLE_128B, K-major: step kk starts 32 bytes further along a
-// 128-byte row; steps 4-7 read the second half).
+// S[128 q][128 k] = Q . K^T: HD/16 K=16 steps over the 64-column halves of Q
+// and K (SWIZZLE_128B, K-major: step kk starts 32 bytes further along a
+// 128-byte row; steps 4-7 read the second half when HD = 128).
 __host__ __device__ constexpr uint32_t s_step(uint32_t kk) { return ((kk >> 2) * kHalf + (kk & 3) * 32) >> 4; }
 __host__ __device__ constexpr uint32_t p_col(uint32_t kk) { return (kk >> 1) * 32 + (kk & 1) * 8; }
 __host__ __device__ constexpr uint32_t v_step(uint32_t kk) { return kk * (2048 >> 4); }
@@ -288,10 +291,10 @@ __device__ __forceinline__ void s_mmas(uint32_t dst, uint64_t qd, uint64_t kd, u
                                        std::integer_sequence<uint32_t, KK...>) {
     (sm100::mma_f16_ss_at<s_step(KK), s_step(KK)>(dst, qd, kd, idesc, KK > 0 ? 1u : 0u), ...);
 }
-// O[128 q][128 d] (+)= P . V with P from TMEM: step kk covers keys 16kk..16kk+15,
+// O[128 q][HD] (+)= P . V with P from TMEM: step kk covers keys 16kk..16kk+15,
 // whose high halves sit in columns 32(kk/2) + 8(kk%2) .. +7 and low halves 16
 // columns further; V (MN-major) advances 16 rows = 2048 bytes per step.  The
-// high-half MMAs run first (the first of a sequence starts the accumulator),
+// high-half MMAs run first (the first of an item starts the accumulator),
 // then the low halves add in.
 template <uint32_t... KK>
 __device__ __forceinline__ void pv_mmas(uint32_t ocol, uint32_t pcol, uint64_t vd, uint32_t idesc,
@@ -333,14 +336,17 @@ __device__ __forceinline__ void add_mask_chunk(uint32_t (&v)[32], const uint16_t
 // taken over raw scores and scaled once).  GEN = true: scores are scaled (and
 // masked) before the max, any finite scale, and rows whose running max
 // becomes +inf give zeros (the SDK CUDA backend's rule for a non-finite max).
-template <typename T, typename OT, bool GEN>
+// HD = head_dim (64 or 128).
+template <typename T, typename OT, bool GEN, int HD>
 __global__ void __launch_bounds__(kPfThreads, 1)
 paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
     using namespace sm100;
+    static_assert(HD == 64 || HD == 128, "head_dim");
+    constexpr int kHalves = HD / 64;          // 64-column halves of a Q/K/V row
     constexpr uint32_t kIdescS = idesc_f16(128, 128, Bf16Flag<T>::value, false, false);
-    constexpr uint32_t kIdescPV = idesc_f16(128, 128, Bf16Flag<T>::value, false, true);
+    constexpr uint32_t kIdescPV = idesc_f16(128, HD, Bf16Flag<T>::value, false, true);
     extern __shared__ unsigned char smem_raw[];
     unsigned char *sm = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -408,16 +414,17 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             if (I.ntiles == 0) continue;
             if (!mbar_wait(q_empty, (qi & 1) ^ 1, abort_flag, fault)) break;
             if (lane == 0) {
-                mbar_arrive_expect_tx(q_full, (paired ? 4u : 2u) * kHalf);
+                mbar_arrive_expect_tx(q_full, (paired ? 2u : 1u) * kHalves * kHalf);
                 // token-major rows: (column, head, row); dense: (column, row, head)
                 const int32_t c1 = a.dense_layout ? I.qrel : I.h0;
                 const int32_t c2 = a.dense_layout ? (a.seq0 + I.b) * a.q_heads + I.h0 : I.q0;
                 const int32_t d1 = a.dense_layout ? 0 : 1, d2 = a.dense_layout ? 1 : 0;
-                tma_load_3d(sm + kQOff, &qmap, q_full, 0, c1, c2);
-                tma_load_3d(sm + kQOff + kHalf, &qmap, q_full, 64, c1, c2);
-                if (paired) {
-                    tma_load_3d(sm + kQOff + 2 * kHalf, &qmap, q_full, 0, c1 + d1, c2 + d2);
-                    tma_load_3d(sm + kQOff + 3 * kHalf, &qmap, q_full, 64, c1 + d1, c2 + d2);
+#pragma unroll
+                for (int hf = 0; hf < kHalves; ++hf) {
+                    tma_load_3d(sm + kQOff + hf * kHalf, &qmap, q_full, 64 * hf, c1, c2);
+                    if (paired)
+                        tma_load_3d(sm + kQOff + (2 + hf) * kHalf, &qmap, q_full, 64 * hf,
+                                    c1 + d1, c2 + d2);
                 }
             }
             __syncwarp();
@@ -438,9 +445,9 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     if (!good) record_fault(fault, kFaultPageOutOfRange);
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, good);
-                const uint32_t bytes = (uint32_t)__popc(mask) * a.block_size * 256u;
+                const uint32_t bytes = (uint32_t)__popc(mask) * a.block_size * (2u * HD);
                 const uint32_t ro = (uint32_t)lane * a.block_size * 128u;
-                const int32_t y = (int32_t)pid * a.block_size, x = I.g * 128;
+                const int32_t y = (int32_t)pid * a.block_size, x = I.g * HD;
                 const int st = (int)(jj % kStages);
                 const uint32_t par = ((jj / kStages) & 1) ^ 1;
                 if (!mbar_wait(&kempty[st], par, abort_flag, fault)) {
@@ -451,8 +458,9 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 __syncwarp();
                 if (good) {
                     unsigned char *kst = sm + kKOff + st * 32768;
-                    tma_load_2d(kst + ro, &kmap, &kfull[st], x, y);
-                    tma_load_2d(kst + kHalf + ro, &kmap, &kfull[st], x + 64, y);
+#pragma unroll
+                    for (int hf = 0; hf < kHalves; ++hf)
+                        tma_load_2d(kst + hf * kHalf + ro, &kmap, &kfull[st], x + 64 * hf, y);
                 }
                 if (!mbar_wait(&vempty[st], par, abort_flag, fault)) {
                     ok = false;
@@ -462,8 +470,9 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 __syncwarp();
                 if (good) {
                     unsigned char *vst = sm + kVOff + st * 32768;
-                    tma_load_2d(vst + ro, &vmap, &vfull[st], x, y);
-                    tma_load_2d(vst + kHalf + ro, &vmap, &vfull[st], x + 64, y);
+#pragma unroll
+                    for (int hf = 0; hf < kHalves; ++hf)
+                        tma_load_2d(vst + hf * kHalf + ro, &vmap, &vfull[st], x + 64 * hf, y);
                 }
             }
             ++qi;
@@ -491,7 +500,8 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             auto issue_s = [&](int w, uint32_t t) -> bool {
                 const uint64_t qd = qdesc + (uint64_t)((uint32_t)w * (2 * kHalf >> 4));
                 const uint64_t kd = kdesc + (uint64_t)((t % kStages) * (32768u >> 4));
-                s_mmas(sbuf(w, t), qd, kd, kIdescS, std::make_integer_sequence<uint32_t, 8>{});
+                s_mmas(sbuf(w, t), qd, kd, kIdescS,
+                       std::make_integer_sequence<uint32_t, HD / 16>{});
                 mma_commit(&s_full[w]);
                 return true;
             };
@@ -616,10 +626,11 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     if (k0 + r >= I.L) {
                         unsigned char *vrow = sm + kVOff + st * 32768 + r * 128;
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            reinterpret_cast<uint4 *>(vrow)[i] = make_uint4(0, 0, 0, 0);
-                            reinterpret_cast<uint4 *>(vrow + kHalf)[i] = make_uint4(0, 0, 0, 0);
-                        }
+                        for (int hf = 0; hf < kHalves; ++hf)
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                reinterpret_cast<uint4 *>(vrow + hf * kHalf)[i] =
+                                    make_uint4(0, 0, 0, 0);
                     }
                     fence_proxy_async_smem();
                 }
@@ -628,7 +639,7 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                     if (!wait(&pv_done[w], (jj - 1) & 1)) { ok = false; break; }
                     tc_fence_after();
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < HD / 32; ++c) {
                         uint32_t o[32];
                         tmem_ld_32x32b_x32(ocol + c * 32, o);
                         tmem_wait_ld();
@@ -691,10 +702,10 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
             OT *orow = static_cast<OT *>(a.out) +
                        (a.dense_layout
                             ? (((int64_t)(a.seq0 + I.b) * a.q_heads + I.h0 + w) * a.dense_rows +
-                               I.qrel + r) * 128
-                            : ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * 128);
+                               I.qrel + r) * HD
+                            : ((int64_t)(I.q0 + r) * a.q_heads + I.h0 + w) * HD);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < HD / 32; ++c) {
                 uint32_t o[32];
                 tmem_ld_32x32b_x32(ocol + c * 32, o);
                 tmem_wait_ld();
@@ -734,10 +745,10 @@ int sms() {
     return g_sms[dev];
 }
 
-template <typename T, typename OT, bool GEN>
+template <typename T, typename OT, bool GEN, int HD>
 int launch(const PfArgs &args, const CUtensorMap &qm, const CUtensorMap &km,
            const CUtensorMap &vm, cudaStream_t s) {
-    auto kern = paged_prefill_tc_kernel<T, OT, GEN>;
+    auto kern = paged_prefill_tc_kernel<T, OT, GEN, HD>;
     static int configured[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -749,6 +760,24 @@ int launch(const PfArgs &args, const CUtensorMap &qm, const CUtensorMap &km,
     }
     kern<<<sms(), kPfThreads, pf_smem_bytes(args.batch), s>>>(args, qm, km, vm);
     return cudaGetLastError() == cudaSuccess;
+}
+
+template <typename T, typename OT, int HD>
+int launch_gen(bool gen, const PfArgs &args, const CUtensorMap &qm, const CUtensorMap &km,
+               const CUtensorMap &vm, cudaStream_t s) {
+    return gen ? launch<T, OT, true, HD>(args, qm, km, vm, s)
+               : launch<T, OT, false, HD>(args, qm, km, vm, s);
+}
+
+template <int HD>
+int launch_typed(bool bf16, PkvDType out, bool gen, const PfArgs &args, const CUtensorMap &qm,
+                 const CUtensorMap &km, const CUtensorMap &vm, cudaStream_t s) {
+    if (!bf16)
+        return out == PKV_DTYPE_F32 ? launch_gen<__half, float, HD>(gen, args, qm, km, vm, s)
+                                    : launch_gen<__half, __half, HD>(gen, args, qm, km, vm, s);
+    return out == PKV_DTYPE_F32
+               ? launch_gen<__nv_bfloat16, float, HD>(gen, args, qm, km, vm, s)
+               : launch_gen<__nv_bfloat16, __nv_bfloat16, HD>(gen, args, qm, km, vm, s);
 }
 
 }  // namespace
@@ -791,11 +820,12 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
     }
     const size_t kvh = layer->kv_heads;
     const size_t bs = layer->block_size;
-    if (layer->head_dim != 128 || kvh == 0 || q_heads == 0 || q_heads % kvh != 0 ||
+    const size_t hd = layer->head_dim;
+    if ((hd != 64 && hd != 128) || kvh == 0 || q_heads == 0 || q_heads % kvh != 0 ||
         q_heads > 65535 || (bs != 16 && bs != 32 && bs != 64 && bs != 128)) {
         pkv_internal_set_error(error, error_capacity,
-                               "%s: needs head_dim 128, q_heads a multiple of kv_heads and pages "
-                               "of 16, 32, 64 or 128 tokens",
+                               "%s: needs head_dim 64 or 128, q_heads a multiple of kv_heads and "
+                               "pages of 16, 32, 64 or 128 tokens",
                                what);
         return 0;
     }
@@ -825,14 +855,14 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
         // token-major [rows][q_heads][128], or dense [sequences * q_heads]
         // [max_query_len][128] with every sequence holding max_query_len rows
         const uint64_t nseq_heads = dense_layout ? total_query_rows / max_query_len * q_heads : 0;
-        cuuint64_t dims[3] = {128, q_heads, total_query_rows};
-        cuuint64_t strides[2] = {256, q_heads * 256};
+        cuuint64_t dims[3] = {hd, q_heads, total_query_rows};
+        cuuint64_t strides[2] = {hd * 2, q_heads * hd * 2};
         cuuint32_t box[3] = {64, 1, 128};
         if (dense_layout) {
             dims[1] = max_query_len;
             dims[2] = nseq_heads;
-            strides[0] = 256;
-            strides[1] = max_query_len * 256;
+            strides[0] = hd * 2;
+            strides[1] = max_query_len * hd * 2;
             box[1] = 128;
             box[2] = 1;
         }
@@ -845,8 +875,8 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
         }
     }
     for (int i = 0; i < 2; ++i) {
-        cuuint64_t dims[2] = {kvh * 128, rows};
-        cuuint64_t strides[1] = {kvh * 256};
+        cuuint64_t dims[2] = {kvh * hd, rows};
+        cuuint64_t strides[1] = {kvh * hd * 2};
         cuuint32_t box[2] = {64, (cuuint32_t)bs};
         cuuint32_t es[2] = {1, 1};
         if (enc(i == 0 ? &km : &vm, dt, 2, i == 0 ? layer->key_pool : layer->value_pool, dims,
@@ -887,18 +917,8 @@ int pkv_internal_paged_prefill_ex(const PkvPagedLayer *layer, const PkvBatch *ba
         sl.seq_lens = batch->seq_lens + b0;
         sl.q_offsets = query_offsets + b0;  // absolute row offsets: query/out stay global
         sl.out = output;
-        if (!bf16)
-            ok = output_dtype == PKV_DTYPE_F32
-                     ? (gen ? pkv::launch<__half, float, true>(sl, qm, km, vm, s)
-                            : pkv::launch<__half, float, false>(sl, qm, km, vm, s))
-                     : (gen ? pkv::launch<__half, __half, true>(sl, qm, km, vm, s)
-                            : pkv::launch<__half, __half, false>(sl, qm, km, vm, s));
-        else
-            ok = output_dtype == PKV_DTYPE_F32
-                     ? (gen ? pkv::launch<__nv_bfloat16, float, true>(sl, qm, km, vm, s)
-                            : pkv::launch<__nv_bfloat16, float, false>(sl, qm, km, vm, s))
-                     : (gen ? pkv::launch<__nv_bfloat16, __nv_bfloat16, true>(sl, qm, km, vm, s)
-                            : pkv::launch<__nv_bfloat16, __nv_bfloat16, false>(sl, qm, km, vm, s));
+        ok = hd == 128 ? pkv::launch_typed<128>(bf16, output_dtype, gen, sl, qm, km, vm, s)
+                       : pkv::launch_typed<64>(bf16, output_dtype, gen, sl, qm, km, vm, s);
     }
     if (!ok) {
         pkv_internal_set_error(error, error_capacity, "%s: launch failed: %s", what,

@@ -113,28 +113,33 @@ def test_kernel_entry_points_reject_bad_arguments(lib):
 
 def test_dense_and_selftest_entry_points_reject_bad_arguments(lib):
     """Validation that happens before any device work (no GPU needed)."""
+    f = ctypes.c_float
     e = _err()
-    assert lib.pkv_sdpa_f16(None, None, None, None, None, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 1,
+    assert lib.pkv_sdpa_f16(None, None, None, None, None, 1, 8, 2, 4, 4, 128, f(0.1), 1,
                             None, 0, None, e, len(e)) == 0
     assert b"null" in e.value
     e = _err()  # q_heads not a multiple of kv_heads
-    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 6, 4, 4, 4, ctypes.c_float(0.1), 1, 256,
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 6, 4, 4, 4, 128, f(0.1), 1, 256,
                             1 << 20, None, e, len(e)) == 0
     assert b"multiple" in e.value
     e = _err()  # non-finite scale
-    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(float("inf")), 1,
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 128, f(float("inf")), 1,
                             256, 1 << 20, None, e, len(e)) == 0
     assert b"finite" in e.value
     e = _err()  # causal must be 0 or 1
-    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 2, 256,
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 128, f(0.1), 2, 256,
                             1 << 20, None, e, len(e)) == 0
+    e = _err()  # head_dim must be 64 or 128
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 96, f(0.1), 1, 256,
+                            1 << 20, None, e, len(e)) == 0
+    assert b"head_dim" in e.value
     e = _err()  # workspace too small
-    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, ctypes.c_float(0.1), 1, 256, 8,
+    assert lib.pkv_sdpa_f16(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 64, f(0.1), 1, 256, 8,
                             None, e, len(e)) == 0
     assert b"workspace" in e.value
-    # the host hook refuses head_dim / value_dim other than 128 (returns 0)
-    assert lib.pkv_sdpa_f16_host(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 64, 64, ctypes.c_float(0.1),
-                                 1) == 0
+    # the host hook refuses head_dim other than 64 / 128 and value_dim != head_dim
+    assert lib.pkv_sdpa_f16_host(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 96, 96, f(0.1), 1) == 0
+    assert lib.pkv_sdpa_f16_host(16, 16, 16, None, 16, 1, 8, 2, 4, 4, 128, 64, f(0.1), 1) == 0
     e = _err()
     assert lib.pkv_selftest_wait_timeout(None, e, len(e)) == 0
     assert b"null" in e.value

@@ -20,10 +20,10 @@ from tests.gpu_cases import check_close
 pytestmark = pytest.mark.gpu
 
 
-def case(B, Hq, Hkv, Lq, Lk, seed):
+def case(B, Hq, Hkv, Lq, Lk, seed, d=128):
     rng = np.random.default_rng(seed)
     f = lambda *shape: rng.standard_normal(shape).astype(np.float16)
-    return f(B, Hq, Lq, 128), f(B, Hkv, Lk, 128), f(B, Hkv, Lk, 128)
+    return f(B, Hq, Lq, d), f(B, Hkv, Lk, d), f(B, Hkv, Lk, d)
 
 
 def expected(q, k, v, scale, causal, oracle_mod):
@@ -192,8 +192,55 @@ def test_positive_infinite_mask_row(lib, oracle_mod, cuda):
 
 
 def test_refused_shapes(lib, cuda):
+    q, k, v = case(1, 4, 2, 32, 16, seed=1, d=96)
+    assert P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v.view(np.uint16), 0.1,
+                           True) is None  # head_dim 96
     q, k, v = case(1, 4, 2, 32, 16, seed=1)
-    q64 = np.ascontiguousarray(q[..., :64])
-    k64, v64 = np.ascontiguousarray(k[..., :64]), np.ascontiguousarray(v[..., :64])
-    assert P.sdpa_f16_host(q64.view(np.uint16), k64.view(np.uint16), v64.view(np.uint16), 0.1,
-                           True) is None  # head_dim 64
+    v64 = np.ascontiguousarray(v[..., :64])
+    assert P.sdpa_f16_host(q.view(np.uint16), k.view(np.uint16), v64.view(np.uint16), 0.1,
+                           True) is None  # value_dim 64 != head_dim 128
+
+
+# ---- head_dim 64 (SmolVLM-class text models: the SDK's callers read head_dim
+# from the model config, tests/smolvlm/src/app/text_model.c:603-604) ----
+
+@pytest.mark.parametrize("B,Hq,Hkv,Lq,Lk,causal", [
+    (1, 4, 1, 1, 1, True),
+    (2, 9, 3, 100, 300, True),    # kv_len not a multiple of 16, odd group (3)
+    (2, 8, 2, 256, 256, True),    # the tensors are the page pool
+    (1, 8, 8, 130, 400, False),   # MHA, no causal mask
+    (1, 4, 1, 300, 100, True),    # q_len > kv_len
+])
+def test_head_dim_64_device_entry(lib, oracle_mod, cuda, B, Hq, Hkv, Lq, Lk, causal):
+    import torch
+    q, k, v = case(B, Hq, Hkv, Lq, Lk, seed=B * 31 + Lq, d=64)
+    scale = 0.125
+    dq, dk, dv = (torch.from_numpy(a).to(cuda) for a in (q, k, v))
+    out = torch.empty_like(dq)
+    P.sdpa_f16(dq, dk, dv, out, scale, causal)
+    torch.cuda.synchronize()
+    check_close(out.float().cpu().numpy(), expected(q, k, v, scale, causal, oracle_mod),
+                f"d=64 B={B} Hq={Hq} Hkv={Hkv} Lq={Lq} Lk={Lk} causal={causal}")
+    assert P.device_fault(0) == 0
+
+
+def test_head_dim_64_host_hook_with_mask_against_sdk(lib, oracle_mod, cuda):
+    """The run_f16 hook at head_dim 64 with an additive mask: against the
+    restatement, the SDK's own tensor_sdpa_f32 and its CUDA run_f16."""
+    q, k, v = case(2, 8, 2, 96, 250, seed=64, d=64)
+    mask = make_mask(96, 250, seed=65, dead_rows=(7,))
+    bits = (q.view(np.uint16), k.view(np.uint16), v.view(np.uint16))
+    got = P.sdpa_f16_host(*bits, 0.125, True, mask=mask.view(np.uint16))
+    assert got is not None
+    got = got.view(np.float16).astype(np.float32)
+    f32 = (q.astype(np.float32), k.astype(np.float32), v.astype(np.float32))
+    check_close(got, oracle_mod.sdpa_f32(*f32, 0.125, True, mask=mask.astype(np.float32)),
+                "d=64 host hook vs oracle")
+    assert not got[:, :, 7].any()
+    if O.ref_available():
+        check_close(got, O.ref_sdpa_f32(*f32, 0.125, True, mask=mask.astype(np.float32)),
+                    "d=64 host hook vs SDK tensor_sdpa_f32")
+    if O.ref_cuda_available():
+        ref = O.ref_cuda_sdpa_f16(*bits, 0.125, True, mask=mask.view(np.uint16))
+        assert ref is not None
+        check_close(got, ref.view(np.float16).astype(np.float32), "d=64 host hook vs SDK CUDA")

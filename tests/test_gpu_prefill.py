@@ -25,21 +25,22 @@ class PrefillCase:
     """Pools holding `past` context tokens plus each sequence's new chunk."""
 
     def __init__(self, past, chunk, q_heads, kv_heads, dtype, seed, device, block_size=16,
-                 streams=(1, 2, 3), pool_pages=None):
+                 streams=(1, 2, 3), pool_pages=None, head_dim=128):
         import torch
         self.past = np.asarray(past, np.int64)
         self.chunk = np.asarray(chunk, np.int64)
         self.lengths = self.past + self.chunk
         self.q_heads, self.kv_heads, self.dtype, self.bs = q_heads, kv_heads, dtype, block_size
+        self.hd = head_dim
         need = int(sum((int(L) + block_size - 1) // block_size for L in self.lengths))
         self.pool_pages = pool_pages or need + 4
         self.tables, _ = W.shuffled_tables(self.lengths, block_size, self.pool_pages, seed)
-        kv = kv_heads * 128
+        kv = kv_heads * head_dim
         rows = self.pool_pages * block_size
         self.kpool = W.normal_bits(seed, (rows, kv), dtype, stream=streams[0])
         self.vpool = W.normal_bits(seed, (rows, kv), dtype, stream=streams[1])
         self.offs = np.concatenate([[0], np.cumsum(self.chunk)]).astype(np.int32)
-        self.q = W.normal_bits(seed, (int(self.offs[-1]), q_heads, 128), dtype,
+        self.q = W.normal_bits(seed, (int(self.offs[-1]), q_heads, head_dim), dtype,
                                stream=streams[2])
         self.device = device
         self.d_k = to_device_bits(self.kpool, dtype, device)
@@ -51,16 +52,16 @@ class PrefillCase:
 
     def run(self, causal=True, out_dtype=None, scale=1 / np.sqrt(128)):
         import torch
-        out = torch.full((int(self.offs[-1]), self.q_heads, 128), float("nan"),
+        out = torch.full((int(self.offs[-1]), self.q_heads, self.hd), float("nan"),
                          dtype=out_dtype or torch.float32, device=self.device)
-        layer = P.make_layer(self.d_k, self.d_v, self.bs, self.kv_heads, 128)
+        layer = P.make_layer(self.d_k, self.d_v, self.bs, self.kv_heads, self.hd)
         P.paged_prefill(layer, P.make_batch(self.d_tab, self.d_len), self.d_q, self.d_offs, out,
                         scale, int(self.chunk.max()), causal)
         torch.cuda.synchronize()
         return out.float().cpu().numpy()
 
     def oracle(self, oracle_mod, causal=True, rows=None, scale=1 / np.sqrt(128)):
-        want = np.zeros((int(self.offs[-1]), self.q_heads, 128), np.float32)
+        want = np.zeros((int(self.offs[-1]), self.q_heads, self.hd), np.float32)
         for b in range(len(self.lengths)):
             sel = np.arange(self.offs[b], self.offs[b + 1]) if rows is None else \
                 np.array([r for r in rows if self.offs[b] <= r < self.offs[b + 1]], np.int64)
@@ -68,7 +69,7 @@ class PrefillCase:
                 continue
             pos = self.past[b] + (sel - self.offs[b])
             want[sel] = oracle_mod.paged_attention_rows(
-                self.q[sel], pos, causal, self.dtype, self.kpool, self.vpool, self.kv_heads, 128,
+                self.q[sel], pos, causal, self.dtype, self.kpool, self.vpool, self.kv_heads, self.hd,
                 self.bs, self.tables[b], int(self.lengths[b]), float(scale))
         return want
 
@@ -92,6 +93,18 @@ def test_prefill_matches_oracle(lib, oracle_mod, cuda, dtype, causal, group):
                        seed=10 + group, device=cuda)
     got = case.run(causal)
     check_close(got, case.oracle(oracle_mod, causal), f"{dtype} causal={causal} group={group}")
+    assert P.device_fault(0) == 0
+
+
+@pytest.mark.parametrize("dtype,causal,group,block", [("bf16", True, 4, 16), ("f16", True, 2, 32),
+                                                      ("bf16", False, 3, 16), ("f16", True, 1, 64)])
+def test_prefill_head_dim_64(lib, oracle_mod, cuda, dtype, causal, group, block):
+    """head_dim 64 (one 64-column half per Q/K/V row, N=64 PV product)."""
+    case = PrefillCase([0, 300, 2100, 37], [200, 129, 130, 1], 2 * group, 2, dtype,
+                       seed=40 + group, device=cuda, block_size=block, head_dim=64)
+    got = case.run(causal, scale=0.125)
+    check_close(got, case.oracle(oracle_mod, causal, scale=0.125),
+                f"d=64 {dtype} causal={causal} group={group} block={block}")
     assert P.device_fault(0) == 0
 
 
