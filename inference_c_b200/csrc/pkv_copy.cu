@@ -40,6 +40,7 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
                int batch, int32_t total_rows, int vec_per_row, int block_size,
                int block_shift, uint32_t block_count, bool tail) {
     pdl_launch_dependents();  // a decode launched after this may set itself up now
+    pdl_wait();               // the kernel before this one (tables, lengths, rows) is done
     const int lane = threadIdx.x & 31;
     const int32_t row = blockIdx.x * kCopyWarps + (threadIdx.x >> 5);
     if (row >= total_rows) return;
@@ -98,17 +99,53 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
     }
 }
 
-__global__ void apply_patches_kernel(uint32_t *table, int64_t stride, int64_t rows,
-                                     const PkvTablePatch *patches, int64_t count) {
+// One step's staging, read straight from the pinned host slot (no copy on
+// the stream): the lengths and row offsets go to the device slot the kernels
+// of the step read, the new page-table entries into the padded table.  One
+// CTA; when it is done it writes `ticket` to the slot's host word, which
+// tells the host the slot may be refilled.
+__global__ void __launch_bounds__(512)
+stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ dev_lens,
+                   int batch, int max_batch, const PkvTablePatch *__restrict__ host_patches,
+                   int64_t count, uint32_t *__restrict__ table, int64_t stride, int64_t rows,
+                   volatile uint32_t *host_done, uint32_t ticket) {
     pdl_launch_dependents();
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    const PkvTablePatch p = patches[i];
-    if ((int64_t)p.row >= rows || (int64_t)p.index >= stride) {
-        record_fault(&g_copy_fault, kFaultPositionOutOfRange);
-        return;
+    pdl_wait();  // the previous step's kernels no longer read the table or this slot
+    for (int i = threadIdx.x; i <= batch; i += blockDim.x) {
+        if (i < batch) dev_lens[i] = host_lens[i];
+        dev_lens[max_batch + i] = host_lens[max_batch + i];
     }
-    table[(int64_t)p.row * stride + p.index] = p.page;
+    for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+        const PkvTablePatch p = host_patches[i];
+        if ((int64_t)p.row >= rows || (int64_t)p.index >= stride) {
+            record_fault(&g_copy_fault, kFaultPositionOutOfRange);
+            continue;
+        }
+        table[(int64_t)p.row * stride + p.index] = p.page;
+    }
+    __syncthreads();  // every read of the host slot has returned
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        *host_done = ticket;
+    }
+}
+
+// Launch with programmatic dependent launch: the kernel may start while the
+// one before it in the stream drains; griddepcontrol.wait inside orders it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                       Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 int block_shift_of(size_t block_size) {
@@ -161,11 +198,12 @@ int launch_rows(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t
     auto *kr = static_cast<uint4 *>(const_cast<void *>(krows));
     auto *vr = static_cast<uint4 *>(const_cast<void *>(vrows));
     const int shift = block_shift_of(layer->block_size);
-#define PKV_ROWS(V)                                                                          \
-    kv_rows_kernel<TO_POOL, V><<<grid, kCopyWarps * 32, 0, (cudaStream_t)stream>>>(          \
-        kp, vp, kr, vr, batch->block_tables, (int32_t)batch->table_stride, batch->seq_lens, \
-        offsets, (int)batch->batch, (int32_t)total_rows, vec, (int)layer->block_size, shift, \
-        (uint32_t)layer->block_count, tail)
+#define PKV_ROWS(V)                                                                           \
+    launch_pdl(kv_rows_kernel<TO_POOL, V>, dim3(grid), dim3(kCopyWarps * 32),                \
+               (cudaStream_t)stream, kp, vp, kr, vr, batch->block_tables,                     \
+               (int32_t)batch->table_stride, batch->seq_lens, offsets, (int)batch->batch,     \
+               (int32_t)total_rows, vec, (int)layer->block_size, shift,                      \
+               (uint32_t)layer->block_count, tail)
     switch (vec) {
         case 32: PKV_ROWS(1); break;    // 512 B rows (e.g. 2 heads x 128)
         case 64: PKV_ROWS(2); break;
@@ -216,13 +254,16 @@ int pkv_kv_gather(const PkvPagedLayer *layer, const PkvBatch *batch, const int32
                                    false, stream, error, error_capacity, "pkv_kv_gather");
 }
 
-int pkv_internal_apply_patches(uint32_t *table, size_t table_stride, size_t table_rows,
-                               const PkvTablePatch *patches, size_t count, PkvStream stream) {
-    if (count == 0) return 1;
-    const unsigned grid = (unsigned)((count + 255) / 256);
-    pkv::apply_patches_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-        table, (int64_t)table_stride, (int64_t)table_rows, patches, (int64_t)count);
-    return cudaGetLastError() == cudaSuccess;
+int pkv_internal_stage_apply(const int32_t *host_lens, int32_t *dev_lens, size_t batch,
+                             size_t max_batch, const PkvTablePatch *host_patches, size_t count,
+                             uint32_t *table, size_t table_stride, size_t table_rows,
+                             uint32_t *host_done, uint32_t ticket, PkvStream stream) {
+    const unsigned threads = count > 256 || batch > 256 ? 512u : 256u;
+    const cudaError_t st = pkv::launch_pdl(
+        pkv::stage_apply_kernel, dim3(1), dim3(threads), (cudaStream_t)stream, host_lens,
+        dev_lens, (int)batch, (int)max_batch, host_patches, (int64_t)count, table,
+        (int64_t)table_stride, (int64_t)table_rows, (volatile uint32_t *)host_done, ticket);
+    return st == cudaSuccess && cudaGetLastError() == cudaSuccess;
 }
 
 // Reads and clears this unit's fault word on the current device.

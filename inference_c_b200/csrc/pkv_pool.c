@@ -13,13 +13,19 @@
  * device work, then set_length(target) on success or set_length(current) on
  * failure, and end_decode.  Unlike the SDK, which re-uploads every block
  * table for every layer on every call (attention_cuda.cu:877-893), the pool
- * keeps one padded device table per batch row and uploads only entries that
- * changed, together with the step's lengths, in one host-to-device copy from
- * pinned memory, once per step for all layers.
+ * keeps one padded device table per batch row and sends only entries that
+ * changed, together with the step's lengths, once per step for all layers:
+ * the host writes them into a pinned, device-mapped staging slot and one
+ * small kernel on the step's stream reads the slot over the bus and applies
+ * it (no copy engine round trip; launched with programmatic dependent launch
+ * so it chains with the append and decode kernels).  That kernel marks the
+ * slot consumed in host memory; the host waits for the mark before it
+ * refills the slot two steps later.
  */
 #include <cuda_runtime_api.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "pkv_b200.h"
 #include "pkv_internal.h"
@@ -43,12 +49,17 @@ struct PkvPool {
     uint32_t *d_tables;           /* [max_batch][max_pages] */
     RowState *rows;
     uint32_t *tmp_pages;          /* max_pages */
-    /* staging: [seq_lens i32 max_batch][row_offsets i32 max_batch+1][pad][patches] */
+    /* staging: [seq_lens i32 max_batch][row_offsets i32 max_batch+1][pad][patches];
+     * h_stage is pinned and device-mapped (h_stage_dev: its device address),
+     * d_stage holds the applied lengths and offsets the kernels read */
     size_t stage_bytes, patch_offset, patch_capacity;
     unsigned char *h_stage[kStageSlots];
+    unsigned char *h_stage_dev[kStageSlots];
     unsigned char *d_stage[kStageSlots];
-    cudaEvent_t stage_done[kStageSlots];
-    int stage_used[kStageSlots];
+    uint32_t *h_consumed;         /* [kStageSlots], pinned and mapped: last ticket applied */
+    uint32_t *h_consumed_dev;
+    uint32_t stage_ticket[kStageSlots];  /* ticket of the slot's last use (0: none) */
+    uint32_t next_ticket;
     int slot;
     /* open step */
     int open;
@@ -70,10 +81,10 @@ static void pool_free_device(PkvPool *p) {
         for (size_t l = 0; l < p->layer_count; ++l) cudaFree(p->vpools[l]);
     cudaFree(p->d_tables);
     for (int s = 0; s < kStageSlots; ++s) {
-        if (p->stage_done[s]) cudaEventDestroy(p->stage_done[s]);
         cudaFreeHost(p->h_stage[s]);
         cudaFree(p->d_stage[s]);
     }
+    cudaFreeHost(p->h_consumed);
     if (have_prev) cudaSetDevice(prev);
 }
 
@@ -161,12 +172,21 @@ int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
     p->patch_offset = align_up((2u * max_batch + 1u) * sizeof(int32_t), 256);
     p->patch_capacity = max_batch * max_pages_per_seq;
     p->stage_bytes = p->patch_offset + p->patch_capacity * sizeof(PkvTablePatch);
+    const unsigned map_flags = cudaHostAllocMapped | cudaHostAllocPortable;
     for (int s = 0; st == cudaSuccess && s < kStageSlots; ++s) {
-        st = cudaHostAlloc((void **)&p->h_stage[s], p->stage_bytes, cudaHostAllocDefault);
-        if (st == cudaSuccess) st = cudaMalloc((void **)&p->d_stage[s], p->stage_bytes);
+        st = cudaHostAlloc((void **)&p->h_stage[s], p->stage_bytes, map_flags);
         if (st == cudaSuccess)
-            st = cudaEventCreateWithFlags(&p->stage_done[s], cudaEventDisableTiming);
+            st = cudaHostGetDevicePointer((void **)&p->h_stage_dev[s], p->h_stage[s], 0);
+        if (st == cudaSuccess)
+            st = cudaMalloc((void **)&p->d_stage[s], p->patch_offset);
     }
+    if (st == cudaSuccess)
+        st = cudaHostAlloc((void **)&p->h_consumed, kStageSlots * sizeof(uint32_t), map_flags);
+    if (st == cudaSuccess) {
+        memset(p->h_consumed, 0, kStageSlots * sizeof(uint32_t));
+        st = cudaHostGetDevicePointer((void **)&p->h_consumed_dev, p->h_consumed, 0);
+    }
+    p->next_ticket = 1;
     if (st == cudaSuccess) st = cudaDeviceSynchronize();
     if (have_prev) cudaSetDevice(prev);
     if (st != cudaSuccess) {
@@ -199,6 +219,28 @@ int pkv_pool_layer(PkvPool *pool, size_t layer, PkvPagedLayer *out) {
     out->head_dim = pool->head_dim;
     out->dtype = pool->dtype;
     return 1;
+}
+
+/* Waits until the kernel that applied the slot's last contents has read
+ * them (it writes its ticket to h_consumed).  Bounded: gives up after about
+ * a minute, or at once when the device reports a sticky error. */
+static int wait_slot_free(PkvPool *p, int slot) {
+    const uint32_t want = p->stage_ticket[slot];
+    volatile const uint32_t *done = p->h_consumed + slot;
+    if (want == 0 || *done == want) return 1;
+    struct timespec t0, now, nap = {0, 20000};
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (unsigned spin = 0;; ++spin) {
+        if (*done == want) return 1;
+        if (spin < 4096) continue;
+        if ((spin & 255u) == 0) {
+            const cudaError_t e = cudaPeekAtLastError();
+            if (e != cudaSuccess && e != cudaErrorNotReady) return 0;
+            clock_gettime(CLOCK_MONOTONIC, &now);
+            if (now.tv_sec - t0.tv_sec > 60) return 0;
+        }
+        nanosleep(&nap, NULL);
+    }
 }
 
 /* Undo the first `n` sequences of a half-opened step. */
@@ -262,7 +304,14 @@ int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
     }
     /* 3. stage lengths, row offsets and table patches */
     const int slot = p->slot;
-    if (p->stage_used[slot]) cudaEventSynchronize(p->stage_done[slot]);
+    if (!wait_slot_free(p, slot)) {
+        rollback(p, batch, 1);
+        pkv_internal_set_error(error, cap,
+                               "pkv_step_begin: staging slot still in use (device stalled or "
+                               "failed: %s)",
+                               cudaGetErrorString(cudaPeekAtLastError()));
+        return 0;
+    }
     int32_t *lens = (int32_t *)p->h_stage[slot];
     int32_t *offs = lens + p->max_batch;
     PkvTablePatch *patches = (PkvTablePatch *)(p->h_stage[slot] + p->patch_offset);
@@ -304,19 +353,18 @@ int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
     int prev = 0;
     const int have_prev = cudaGetDevice(&prev) == cudaSuccess;
     cudaSetDevice(p->device);
-    const cudaStream_t s = (cudaStream_t)stream;
-    /* one copy: lengths + offsets (+ patches when any) */
-    size_t bytes = npatch ? p->patch_offset + npatch * sizeof(PkvTablePatch)
-                          : (2u * p->max_batch + 1u) * sizeof(int32_t);
-    cudaError_t st = cudaMemcpyAsync(p->d_stage[slot], p->h_stage[slot], bytes,
-                                     cudaMemcpyHostToDevice, s);
-    if (st == cudaSuccess) st = cudaEventRecord(p->stage_done[slot], s);
-    p->stage_used[slot] = 1;
-    if (st == cudaSuccess && npatch &&
-        !pkv_internal_apply_patches(p->d_tables, p->max_pages, p->max_batch,
-                                    (const PkvTablePatch *)(p->d_stage[slot] + p->patch_offset),
-                                    npatch, stream))
+    /* one kernel reads the slot and applies it */
+    const uint32_t ticket = p->next_ticket;
+    p->next_ticket = p->next_ticket + 1u == 0u ? 1u : p->next_ticket + 1u;
+    cudaError_t st = cudaSuccess;
+    if (!pkv_internal_stage_apply((const int32_t *)p->h_stage_dev[slot],
+                                  (int32_t *)p->d_stage[slot], batch, p->max_batch,
+                                  (const PkvTablePatch *)(p->h_stage_dev[slot] + p->patch_offset),
+                                  npatch, p->d_tables, p->max_pages, p->max_batch,
+                                  p->h_consumed_dev + slot, ticket, stream))
         st = cudaErrorLaunchFailure;
+    else
+        p->stage_ticket[slot] = ticket;
     if (have_prev) cudaSetDevice(prev);
     if (st != cudaSuccess) {
         for (size_t b = 0; b < batch; ++b) p->rows[b].seq = 0;
