@@ -783,28 +783,23 @@ def run_cfg4(args) -> None:
     max_len = L0 + grow
     ws = P.decode_workspace(1, qhl, c.head_dim, max_len, device=dev)
     stream = torch.cuda.current_stream()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4 * steps)]
     cur = [L0]
 
-    def step(i=None, q_in=None):
+    def step(q_in=None, k_in=None, v_in=None, full_out=None):
+        """Transaction, append, decode of this rank's heads, then the NCCL
+        all-gather of every rank's head outputs.  No events between the
+        kernels, so their launches overlap (programmatic dependent launch)."""
         pool.step_begin([seq], [1])
         b = pool.step_batch()
-        P.kv_append(layer, b, newk, newv)
-        if i is not None:
-            ev[4 * i].record(stream)
+        P.kv_append(layer, b, newk if k_in is None else k_in, newv if v_in is None else v_in)
         P.paged_decode(layer, b, q if q_in is None else q_in, out, c.scale, max_len, ws)
-        if i is not None:
-            ev[4 * i + 1].record(stream)
         pool.step_end(True)
         cur[0] += 1
+        dst = full if full_out is None else full_out
         if dist is not None:
-            if i is not None:
-                ev[4 * i + 2].record(stream)
-            dist.all_gather_into_tensor(full, out)  # per-head outputs over NVLink
-            if i is not None:
-                ev[4 * i + 3].record(stream)
+            dist.all_gather_into_tensor(dst, out)  # per-head outputs over NVLink
         else:
-            full.copy_(out)
+            dst.copy_(out)
 
     def barrier():
         torch.cuda.synchronize()
@@ -818,6 +813,23 @@ def run_cfg4(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def timed(fn, k, align=False):
+        """Mean device ms of fn() over k calls, CUDA events on the stream;
+        align: barrier + synchronize before each call (no rank skew)."""
+        ms = []
+        for _ in range(k):
+            if align:
+                barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            if align:
+                torch.cuda.synchronize()
+            ms.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(x.elapsed_time(y) for x, y in ms)
+
     sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
     with sampler:
         for _ in range(warmup):
@@ -826,42 +838,73 @@ def run_cfg4(args) -> None:
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for i in range(steps):
-            step(i)
+            step()
         t1.record(stream)
         barrier()
         ms = max_over_ranks(t0.elapsed_time(t1) / steps)
-        dec = statistics.mean(ev[4 * i].elapsed_time(ev[4 * i + 1]) for i in range(steps))
-        ag = (statistics.mean(ev[4 * i + 2].elapsed_time(ev[4 * i + 3]) for i in range(steps))
+        # the decode kernel(s) alone (open step, no new token), and the
+        # all-gather alone after a barrier (its latency without rank skew)
+        pool.step_begin([seq], [0])
+        b0 = pool.step_batch()
+        dec = timed(lambda: P.paged_decode(layer, b0, q, out, c.scale, max_len, ws), steps)
+        pool.step_end(True)
+        ag = (timed(lambda: dist.all_gather_into_tensor(full, out), steps, align=True)
               if dist is not None else 0.0)
-        h_q = torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
-        h_k = torch.empty(newk.shape, dtype=newk.dtype, pin_memory=True).copy_(newk.cpu())
-        h_v = torch.empty(newv.shape, dtype=newv.dtype, pin_memory=True).copy_(newv.cpu())
-        h_o = torch.empty(full.shape, dtype=full.dtype, pin_memory=True)
-        dq = torch.empty_like(q)
+        # e2e: host buffers, double-buffered on a copy stream (as config 3)
+        copy = torch.cuda.Stream(device=dev)
+        h_q = [torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
+               for _ in range(2)]
+        h_k = [torch.empty(newk.shape, dtype=newk.dtype, pin_memory=True).copy_(newk.cpu())
+               for _ in range(2)]
+        h_v = [torch.empty(newv.shape, dtype=newv.dtype, pin_memory=True).copy_(newv.cpu())
+               for _ in range(2)]
+        h_o = [torch.empty(full.shape, dtype=full.dtype, pin_memory=True) for _ in range(2)]
+        d_q = [torch.empty_like(q) for _ in range(2)]
+        d_k = [torch.empty_like(newk) for _ in range(2)]
+        d_v = [torch.empty_like(newv) for _ in range(2)]
+        d_f = [torch.empty_like(full) for _ in range(2)]
+        up_done = [torch.cuda.Event() for _ in range(2)]
+        step_done = [torch.cuda.Event() for _ in range(2)]
+        used = [False, False]
 
-        def e2e_step():
-            dq.copy_(h_q, non_blocking=True)
-            newk.copy_(h_k, non_blocking=True)
-            newv.copy_(h_v, non_blocking=True)
-            step(None, dq)
-            h_o.copy_(full, non_blocking=True)
-            stream.synchronize()
+        def upload(s_):
+            with torch.cuda.stream(copy):
+                if used[s_]:
+                    copy.wait_event(step_done[s_])
+                d_q[s_].copy_(h_q[s_], non_blocking=True)
+                d_k[s_].copy_(h_k[s_], non_blocking=True)
+                d_v[s_].copy_(h_v[s_], non_blocking=True)
+                up_done[s_].record(copy)
 
-        for _ in range(warmup):
-            e2e_step()
+        def e2e_run(k):
+            upload(0)
+            for i in range(k):
+                s_ = i & 1
+                if i + 1 < k:
+                    upload(s_ ^ 1)
+                stream.wait_event(up_done[s_])
+                step(d_q[s_], d_k[s_], d_v[s_], d_f[s_])
+                step_done[s_].record(stream)
+                used[s_] = True
+                with torch.cuda.stream(copy):
+                    copy.wait_event(step_done[s_])
+                    h_o[s_].copy_(d_f[s_], non_blocking=True)
+
+        e2e_run(warmup)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(steps):
-            e2e_step()
+        e2e_run(steps)
+        stream.wait_stream(copy)
         e1.record(stream)
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        h_q, h_k, h_v, h_o = h_q[0], h_k[0], h_v[0], h_o[0]
     fault = P.device_fault(local)
     if fault:
         raise SystemExit(f"device fault code {fault} recorded during the bench")
     peak, peak_kind = peak_hbm()
-    alg = (L0 + warmup + steps) * kv * 2 * 2 + 2 * q.numel() * 2
+    alg = cur[0] * kv * 2 * 2 + 2 * q.numel() * 2  # the decode-only launches' length
     gbs = alg / (dec / 1e3) / 1e9
     if rank == 0:
         line = {
@@ -881,11 +924,13 @@ def run_cfg4(args) -> None:
                          "kernel": "paged_decode_tc_kernel (+ merge kernel when split wide)",
                          "algorithmic_bytes_per_launch": alg, "mean_launch_ms": dec},
             "allgather_ms": ag,
+            "allgather_timing": "NCCL all_gather_into_tensor alone, each call after a barrier "
+                                "and synchronize (latency without rank skew)",
             "cpu_baseline": None,
             "e2e": {"value": 1.0 / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": (h_q.numel() + h_k.numel() + h_v.numel()) * 2 * world,
                     "d2h_bytes_per_step": h_o.numel() * 2},
-            "gpu_launches": steps * (3 + (1 if dist is not None else 0)),
+            "gpu_launches": steps * 4,  # staging, append, decode, merge (+ NCCL's kernel)
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
