@@ -10,6 +10,7 @@
 
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 
 namespace pkv {
 namespace {
@@ -236,6 +237,7 @@ void pkv_internal_set_error(char *error, size_t capacity, const char *fmt, ...) 
 int pkv_kv_append(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
                   const void *key_rows, const void *value_rows, size_t total_rows,
                   PkvStream stream, char *error, size_t error_capacity) {
+    PKV_RANGE("pkv_kv_append");
     return pkv::launch_rows<true>(layer, batch, row_offsets, key_rows, value_rows, total_rows,
                                   true, stream, error, error_capacity, "pkv_kv_append");
 }
@@ -243,6 +245,7 @@ int pkv_kv_append(const PkvPagedLayer *layer, const PkvBatch *batch, const int32
 int pkv_kv_import(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
                   const void *key_rows, const void *value_rows, size_t total_rows,
                   PkvStream stream, char *error, size_t error_capacity) {
+    PKV_RANGE("pkv_kv_import");
     return pkv::launch_rows<true>(layer, batch, row_offsets, key_rows, value_rows, total_rows,
                                   false, stream, error, error_capacity, "pkv_kv_import");
 }
@@ -250,6 +253,7 @@ int pkv_kv_import(const PkvPagedLayer *layer, const PkvBatch *batch, const int32
 int pkv_kv_gather(const PkvPagedLayer *layer, const PkvBatch *batch, const int32_t *row_offsets,
                   void *key_out, void *value_out, size_t total_rows, PkvStream stream,
                   char *error, size_t error_capacity) {
+    PKV_RANGE("pkv_kv_gather");
     return pkv::launch_rows<false>(layer, batch, row_offsets, key_out, value_out, total_rows,
                                    false, stream, error, error_capacity, "pkv_kv_gather");
 }

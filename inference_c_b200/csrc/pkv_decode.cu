@@ -42,6 +42,7 @@
 
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 #include "pkv_sm100.cuh"
 
 namespace pkv {
@@ -1322,6 +1323,7 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
                      size_t max_seq_len, size_t chunk_tokens, void *workspace,
                      size_t workspace_bytes, PkvStream stream, char *error,
                      size_t error_capacity) {
+    PKV_RANGE("pkv_paged_decode");
     const char *what = "pkv_paged_decode";
     if (layer == nullptr || batch == nullptr || query == nullptr || output == nullptr ||
         layer->key_pool == nullptr || layer->value_pool == nullptr ||
@@ -1573,6 +1575,7 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
                                                void *output, PkvDType output_dtype,
                                                size_t max_seq_len, PkvStream stream, char *error,
                                                size_t error_capacity) {
+    PKV_RANGE("pkv_paged_decode_static_scratch");
     const char *what = "pkv_paged_decode_static_scratch";
     // Everything the scratch size depends on is checked before the array is
     // touched, so a refused call writes no device memory.

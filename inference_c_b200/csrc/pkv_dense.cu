@@ -30,6 +30,7 @@
 
 #include "pkv_b200.h"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 
 namespace pkv {
 namespace {
@@ -218,6 +219,7 @@ int pkv_sdpa_f16(const void *query, const void *key, const void *value,
                  size_t kv_heads, size_t q_len, size_t kv_len, size_t head_dim, float scale,
                  int causal, void *workspace, size_t workspace_bytes, PkvStream stream,
                  char *error, size_t error_capacity) {
+    PKV_RANGE("pkv_sdpa_f16");
     using namespace pkv;
     const char *what = "pkv_sdpa_f16";
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
@@ -297,6 +299,7 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key, const uint16_t
                       size_t query_heads, size_t kv_heads, size_t query_length,
                       size_t kv_length, size_t head_dim, size_t value_dim, float scale,
                       int causal) {
+    PKV_RANGE("pkv_sdpa_f16_host");
     using namespace pkv;
     if (query == nullptr || key == nullptr || value == nullptr || output == nullptr ||
         !head_dim_ok(head_dim) || value_dim != head_dim || batch == 0 || query_heads == 0 ||

@@ -29,6 +29,7 @@
 
 #include "pkv_b200.h"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 
 enum { kStageSlots = 2 };
 
@@ -253,9 +254,9 @@ static void rollback(PkvPool *p, size_t n, int reserved) {
     }
 }
 
-int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
-                   const size_t *past_lengths, const size_t *new_tokens, size_t batch,
-                   PkvStream stream, char *error, size_t cap) {
+static int step_begin_impl(PkvPool *pool, const TensorPagedKVSequence *sequences,
+                           const size_t *past_lengths, const size_t *new_tokens, size_t batch,
+                           PkvStream stream, char *error, size_t cap) {
     PkvPool *p = pool;
     if (p == NULL || sequences == NULL || new_tokens == NULL) {
         pkv_internal_set_error(error, cap, "pkv_step_begin: null argument");
@@ -377,6 +378,16 @@ int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
     return 1;
 }
 
+int pkv_step_begin(PkvPool *pool, const TensorPagedKVSequence *sequences,
+                   const size_t *past_lengths, const size_t *new_tokens, size_t batch,
+                   PkvStream stream, char *error, size_t cap) {
+    PKV_RANGE_PUSH("pkv_step_begin");
+    const int ok = step_begin_impl(pool, sequences, past_lengths, new_tokens, batch, stream,
+                                   error, cap);
+    PKV_RANGE_POP();
+    return ok;
+}
+
 int pkv_step_batch(PkvPool *pool, PkvBatch *out) {
     if (pool == NULL || out == NULL || !pool->open) return 0;
     out->block_tables = pool->d_tables;
@@ -391,7 +402,7 @@ const int32_t *pkv_step_row_offsets(PkvPool *pool) {
     return (const int32_t *)pool->d_stage[pool->slot] + pool->max_batch;
 }
 
-int pkv_step_end(PkvPool *pool, int commit, char *error, size_t cap) {
+static int step_end_impl(PkvPool *pool, int commit, char *error, size_t cap) {
     PkvPool *p = pool;
     if (p == NULL || !p->open) {
         pkv_internal_set_error(error, cap, "pkv_step_end: no open step");
@@ -412,6 +423,13 @@ int pkv_step_end(PkvPool *pool, int commit, char *error, size_t cap) {
     p->slot = (p->slot + 1) % kStageSlots;
     if (!ok) pkv_internal_set_error(error, cap, "pkv_step_end: commit failed; rolled back");
     return commit ? ok : 1;
+}
+
+int pkv_step_end(PkvPool *pool, int commit, char *error, size_t cap) {
+    PKV_RANGE_PUSH("pkv_step_end");
+    const int ok = step_end_impl(pool, commit, error, cap);
+    PKV_RANGE_POP();
+    return ok;
 }
 
 int pkv_device_fault(int device, uint32_t *code, char *error, size_t cap) {

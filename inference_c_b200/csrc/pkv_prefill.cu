@@ -40,6 +40,7 @@
 
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 #include "pkv_sm100.cuh"
 
 namespace pkv {
@@ -790,6 +791,7 @@ int pkv_paged_prefill(const PkvPagedLayer *layer, const PkvBatch *batch, size_t 
                       size_t max_query_len, float scale, int causal, void *output,
                       PkvDType output_dtype, PkvStream stream, char *error,
                       size_t error_capacity) {
+    PKV_RANGE("pkv_paged_prefill");
     return pkv_internal_paged_prefill_ex(layer, batch, q_heads, query_offsets, query,
                                          total_query_rows, max_query_len, scale, causal, output,
                                          output_dtype, nullptr, 0, 0, 0, stream, error,

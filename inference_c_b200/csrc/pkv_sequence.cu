@@ -47,6 +47,7 @@
 #include "pkv_b200.h"
 #include "pkv_device.cuh"
 #include "pkv_internal.h"
+#include "pkv_trace.h"
 
 namespace pkv {
 namespace {
@@ -951,6 +952,7 @@ int pkv_internal_take_sequence_fault(uint32_t *code) {
 }
 
 int tensor_attention_decode_sequence_paged(const TensorPagedKVDecodeRequest *request) {
+    PKV_RANGE("tensor_attention_decode_sequence_paged");
     using namespace pkv;
     if (!valid_request(request)) return 0;
     TensorPagedKVCache *cache = request->cache;
