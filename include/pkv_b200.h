@@ -227,6 +227,41 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key,
                       size_t head_dim, size_t value_dim, float scale, int causal);
 
 /* ---------------------------------------------------------------------- */
+/* Multi-GPU: NCCL all-gather with a host deadline                         */
+/* ---------------------------------------------------------------------- */
+
+/* The SDK has no multi-GPU code (its failure handling is the transaction's
+ * return code and rollback, attention.c:159-166).  For the KV-head split of
+ * one long sequence across GPUs, each GPU decodes its heads and the outputs
+ * are all-gathered with NCCL.  These calls run NCCL in non-blocking mode and
+ * poll it against a deadline, so a peer that never joins or stalls makes
+ * the call return 0 (after ncclCommAbort) instead of hanging; the caller
+ * then ends its step without commit (pkv_step_end(..., 0, ...)), which rolls
+ * the step back.  NCCL is loaded at run time (PKV_NCCL_LIBRARY, default
+ * libnccl.so.2). */
+typedef struct PkvComm PkvComm;
+#define PKV_COMM_ID_BYTES 128
+/* A new communicator id (rank 0 makes it and sends it to the others). */
+int pkv_comm_unique_id(unsigned char *id, size_t id_bytes, char *error, size_t error_capacity);
+/* Joins the communicator of `id` as `rank` of `nranks` on `device`; waits at
+ * most timeout_s seconds for every rank to join. */
+int pkv_comm_init(const unsigned char *id, size_t id_bytes, int nranks, int rank, int device,
+                  double timeout_s, PkvComm **comm, char *error, size_t error_capacity);
+/* Enqueues on `stream` the all-gather of bytes_per_rank bytes from every
+ * rank into recv (rank order); waits at most timeout_s for the enqueue. */
+int pkv_comm_all_gather(PkvComm *comm, const void *send, void *recv, size_t bytes_per_rank,
+                        PkvStream stream, double timeout_s, char *error,
+                        size_t error_capacity);
+/* Waits at most timeout_s for `stream`'s work (the collectives enqueued on
+ * it) to finish, watching NCCL's asynchronous error state; 0 (and the
+ * communicator aborted) on error or timeout. */
+int pkv_comm_wait(PkvComm *comm, PkvStream stream, double timeout_s, char *error,
+                  size_t error_capacity);
+/* 1 when the communicator was aborted (or is NULL): it takes no more work. */
+int pkv_comm_aborted(const PkvComm *comm);
+void pkv_comm_destroy(PkvComm *comm);
+
+/* ---------------------------------------------------------------------- */
 /* 2. Host transaction layer                                               */
 /* ---------------------------------------------------------------------- */
 

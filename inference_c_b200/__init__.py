@@ -159,6 +159,15 @@ EXPORTS = {
     "pkv_step_batch": (_c_int, [_c_ptr, _BP]),
     "pkv_step_row_offsets": (_c_ptr, [_c_ptr]),
     "pkv_step_end": (_c_int, [_c_ptr, _c_int, *_ERR]),
+    # include/pkv_b200.h -- NCCL all-gather with a host deadline
+    "pkv_comm_unique_id": (_c_int, [_c_ptr, _c_size, *_ERR]),
+    "pkv_comm_init": (_c_int, [_c_ptr, _c_size, _c_int, _c_int, _c_int, ctypes.c_double,
+                               ctypes.POINTER(_c_ptr), *_ERR]),
+    "pkv_comm_all_gather": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, ctypes.c_double,
+                                     *_ERR]),
+    "pkv_comm_wait": (_c_int, [_c_ptr, _c_ptr, ctypes.c_double, *_ERR]),
+    "pkv_comm_aborted": (_c_int, [_c_ptr]),
+    "pkv_comm_destroy": (None, [_c_ptr]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -532,3 +541,50 @@ def sdpa_f16_host(query, key, value, scale: float, causal: bool, mask=None):
                                   None if m is None else m.ctypes.data, out.ctypes.data, B, Hq,
                                   Hkv, Lq, Lk, d, dv, ctypes.c_float(scale), int(causal))
     return out if ok else None
+
+
+# ---------------------------------------------------------------------------
+# NCCL all-gather with a host deadline (multi-GPU head split)
+# ---------------------------------------------------------------------------
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    _call("pkv_comm_unique_id", buf, COMM_ID_BYTES)
+    return buf.raw
+
+
+class Comm:
+    """One rank of a non-blocking NCCL communicator (pkv_comm_*): every call
+    waits at most its timeout and raises PkvError (the communicator then
+    aborted) when a peer never joins or stalls."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int,
+                 timeout_s: float):
+        if len(unique_id) != COMM_ID_BYTES:
+            raise ValueError("unique id must be 128 bytes")
+        self._id = ctypes.create_string_buffer(unique_id, COMM_ID_BYTES)
+        h = _c_ptr()
+        _call("pkv_comm_init", self._id, COMM_ID_BYTES, nranks, rank, device,
+              ctypes.c_double(timeout_s), ctypes.byref(h))
+        self.handle = h.value
+
+    def all_gather(self, send, recv, stream=None, timeout_s: float = 10.0) -> None:
+        """send: a CUDA tensor; recv: nranks x send (rank order)."""
+        _call("pkv_comm_all_gather", self.handle, send.data_ptr(), recv.data_ptr(),
+              send.numel() * send.element_size(), _stream_ptr(stream),
+              ctypes.c_double(timeout_s))
+
+    def wait(self, stream=None, timeout_s: float = 10.0) -> None:
+        _call("pkv_comm_wait", self.handle, _stream_ptr(stream), ctypes.c_double(timeout_s))
+
+    @property
+    def aborted(self) -> bool:
+        return bool(load().pkv_comm_aborted(self.handle))
+
+    def destroy(self) -> None:
+        if self.handle:
+            load().pkv_comm_destroy(self.handle)
+            self.handle = None

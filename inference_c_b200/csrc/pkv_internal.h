@@ -56,6 +56,12 @@ int pkv_internal_take_sequence_fault(uint32_t *code);
  * tests only. */
 int pkv_internal_plant_prefill_fault(uint32_t code);
 
+/* Replaces the completion check pkv_comm_wait uses (cudaStreamQuery) with
+ * `probe` (1 done, 0 pending, -1 failed): tests of the deadline logic on
+ * machines without a GPU.  Exported for the tests only. */
+void pkv_internal_comm_set_probe(PkvComm *comm, int (*probe)(void *arg, PkvStream stream),
+                                 void *arg);
+
 /* pkv_paged_prefill with the general options the dense SDPA needs: an
  * additive FP16 mask [query row of the chunk][key] with a row stride in
  * elements (NULL: none), dense mode (a chunk may be longer than its
