@@ -60,6 +60,9 @@ def parse_args():
                    help="wall-time budget of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--comm", choices=["pkv", "torch"], default="pkv",
+                   help="config 4 all-gather: the library's NCCL communicator with a host "
+                        "deadline (pkv_comm_*), or torch.distributed's all_gather_into_tensor")
     p.add_argument("--prefill-batch", type=int, default=0,
                    help="config 5 only: sequences per step (default: the config's 8; smaller "
                         "values make small cases for profiling)")
@@ -739,6 +742,13 @@ def run_cfg4(args) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     P.load()
+    comm = None
+    if dist is not None and args.comm == "pkv":
+        # the library's non-blocking NCCL communicator: a peer that never joins
+        # or stalls ends the wait at the deadline (and the step rolls back)
+        box = [P.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm = P.Comm(box[0], world, rank, local, timeout_s=60.0)
     kvl = c.kv_heads // world                 # KV heads owned by this rank
     qhl = kvl * (c.q_heads // c.kv_heads)     # their query heads
     steps, warmup = args.steps, args.warmup
@@ -796,12 +806,16 @@ def run_cfg4(args) -> None:
         pool.step_end(True)
         cur[0] += 1
         dst = full if full_out is None else full_out
-        if dist is not None:
-            dist.all_gather_into_tensor(dst, out)  # per-head outputs over NVLink
+        if comm is not None:
+            comm.all_gather(out, dst, stream, timeout_s=10.0)  # per-head outputs, NVLink
+        elif dist is not None:
+            dist.all_gather_into_tensor(dst, out)
         else:
             dst.copy_(out)
 
     def barrier():
+        if comm is not None:
+            comm.wait(stream, timeout_s=60.0)  # the collectives of this rank finished
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
@@ -812,6 +826,12 @@ def run_cfg4(args) -> None:
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def gather_only():
+        if comm is not None:
+            comm.all_gather(out, full, stream, timeout_s=10.0)
+        else:
+            dist.all_gather_into_tensor(full, out)
 
     def timed(fn, k, align=False):
         """Mean device ms of fn() over k calls, CUDA events on the stream;
@@ -848,8 +868,7 @@ def run_cfg4(args) -> None:
         b0 = pool.step_batch()
         dec = timed(lambda: P.paged_decode(layer, b0, q, out, c.scale, max_len, ws), steps)
         pool.step_end(True)
-        ag = (timed(lambda: dist.all_gather_into_tensor(full, out), steps, align=True)
-              if dist is not None else 0.0)
+        ag = timed(gather_only, steps, align=True) if dist is not None else 0.0
         # e2e: host buffers, double-buffered on a copy stream (as config 3)
         copy = torch.cuda.Stream(device=dev)
         h_q = [torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
@@ -924,8 +943,11 @@ def run_cfg4(args) -> None:
                          "kernel": "paged_decode_tc_kernel (+ merge kernel when split wide)",
                          "algorithmic_bytes_per_launch": alg, "mean_launch_ms": dec},
             "allgather_ms": ag,
-            "allgather_timing": "NCCL all_gather_into_tensor alone, each call after a barrier "
-                                "and synchronize (latency without rank skew)",
+            "allgather_timing": "the all-gather alone, each call after a barrier and "
+                                "synchronize (latency without rank skew)",
+            "allgather_api": ("pkv_comm_all_gather (non-blocking NCCL communicator, host "
+                              "deadline)" if comm is not None else
+                              "torch.distributed all_gather_into_tensor (NCCL)"),
             "cpu_baseline": None,
             "e2e": {"value": 1.0 / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": (h_q.numel() + h_k.numel() + h_v.numel()) * 2 * world,
@@ -935,6 +957,9 @@ def run_cfg4(args) -> None:
         }
         print(json.dumps(line), flush=True)
     cache.free()
+    if comm is not None:
+        comm.wait(stream, timeout_s=60.0)
+        comm.destroy()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
