@@ -228,7 +228,7 @@ def sdk_cpu_rate(cfg: int, lengths: np.ndarray, budget_s: float, seed: int,
     times = [job.run(threads) for _ in range(repeats)]
     job.close()
     rates = [len(picks) / t for t in times]
-    info = {"cores": threads, "kind": "reference",
+    info = {"cores": min(threads, len(picks)), "kind": "reference",
             "sample": (f"{len(picks)} of {len(lengths)} sequences (stratified by length, "
                        f"{int(lengths[picks].sum())} tokens of context) through the SDK's "
                        f"tensor_sdpa_f32 built from its sources; gather+widen untimed")}
@@ -258,7 +258,8 @@ def run_reference(args) -> None:
         "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) FP16)",
         "impl": "reference",
         "config": config_block(args.config, args.gpus, 0),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+        "cpu_baseline": {"value": value, "unit": "tokens/s",
+                         "cores": min(threads, len(picks)),  # one sequence per thread
                          "kind": "reference",
                          "sample": (f"each step: {len(picks)} of {len(lengths)} sequences "
                                     "(stratified by length) through the SDK's tensor_sdpa_f32 "
