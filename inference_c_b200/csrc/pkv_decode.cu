@@ -501,6 +501,10 @@ struct TcArgs {
     float scale_log2;
     int32_t merge_in_kernel;
     int32_t q_row0;         // query row (sequence * q_heads) of this launch's first sequence
+    // head_dim 64: two KV heads (2g, 2g+1) form one 128-column segment g.
+    // Query heads h < pair_split of a segment use its dims 0-63, the others
+    // dims 64-127; outputs are rows of 64.  0: head_dim 128, rows of 128.
+    int32_t pair_split;
 };
 
 // Tensor maps of one launch: K and V pools (one page x 64 columns per box)
@@ -684,8 +688,11 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
                 }
             }
         }
-        if (pl == 0) {
-            OT *o = out + (f4 >> 5) * 128 + (f4 & 31) * 4;
+        const int hh = f4 >> 5, d = (f4 & 31) * 4;
+        // paired head_dim 64: each head owns one half of the 128 rows
+        const bool owned = a.pair_split == 0 || ((h0 + hh < a.pair_split) == (d < 64));
+        if (pl == 0 && owned) {
+            OT *o = a.pair_split == 0 ? out + hh * 128 + d : out + hh * 64 + (d & 63);
             o[0] = from_f32<OT>(acc.x);
             o[1] = from_f32<OT>(acc.y);
             o[2] = from_f32<OT>(acc.z);
@@ -696,14 +703,22 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
     sync();
 }
 
-template <int G, typename T, typename OT>
+// PAIR (head_dim 64): segment g is KV heads 2g and 2g+1 side by side (128
+// pool columns); its GV = 2G query heads sit in S^T columns 0..G-1 (KV head
+// 2g, Q rows zero in dims 64-127) and 8..8+G-1 (KV head 2g+1, Q rows zero in
+// dims 0-63), so one K . Q^T gives every head its own scores; O^T rows 0-63
+// are the dims of KV head 2g, rows 64-127 those of 2g+1.
+template <int G, typename T, typename OT, bool PAIR>
 __global__ void __launch_bounds__(kTcThreads, 1)
 paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap,
                        const __grid_constant__ CUtensorMap qmap) {
     using namespace sm100;
-    constexpr int GN = G <= 4 ? 4 : G;  // S^T columns read per thread
-    constexpr int PN = G <= 8 ? 16 : 32;  // P^T rows (= O^T columns): hi and lo halves
+    static_assert(!PAIR || G <= 8, "paired heads need G <= 8");
+    constexpr int GV = PAIR ? 2 * G : G;  // query heads of one segment
+    constexpr int GN = PAIR ? 16 : (G <= 4 ? 4 : G);  // S^T columns read per thread
+    constexpr int PN = GV <= 8 ? 16 : 32;  // P^T rows (= O^T columns): hi and lo halves
+    constexpr int OD = PAIR ? 64 : 128;    // output row (head_dim)
     constexpr int LO = PN / 2;
     constexpr uint32_t kPChunk = PN * 128;  // bytes of one 64-token column chunk of P^T
     constexpr uint32_t kIdescQK = idesc_f16(128, 16, IsBf16<T>::value, false, false);
@@ -777,7 +792,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     const bool works = (int)blockIdx.x < ncta && total_tiles > 0;
     const int64_t my_start = works ? range_start(blockIdx.x, ncta, total_tiles) : 0;
     const int64_t my_end = works ? range_start(blockIdx.x + 1, ncta, total_tiles) : 0;
-    const int q_heads = a.kv_heads * G;
+    const int q_heads = a.kv_heads * GV;
     uint32_t *fault = &g_decode_fault;
     if (blockIdx.x == 0 && a.tile_prefix != nullptr)
         for (int b = tid; b <= a.batch; b += kTcThreads) a.tile_prefix[b] = prefix[b];
@@ -823,10 +838,18 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) break;
             if (lane == 0) {  // G query rows, two 64-column halves, 128-byte swizzle
                 unsigned char *qb = sm + kTcQOff + (qi & 1) * 4096;
-                const int32_t qrow = a.q_row0 + P.b * q_heads + P.g * G;
+                const int32_t qrow = a.q_row0 + P.b * q_heads + P.g * GV;
                 mbar_arrive_expect_tx(&q_full[qi & 1], (uint32_t)G * 256u);
-                tma_load_2d(qb, &qmap, &q_full[qi & 1], 0, qrow);
-                tma_load_2d(qb + 2048, &qmap, &q_full[qi & 1], 64, qrow);
+                if constexpr (PAIR) {
+                    // KV head 2g's rows into dims 0-63 at rows 0.., KV head
+                    // 2g+1's into dims 64-127 at rows 8.. (a 1024-byte-aligned
+                    // atom); the rest of the tile stays zero
+                    tma_load_2d(qb, &qmap, &q_full[qi & 1], 0, qrow);
+                    tma_load_2d(qb + 2048 + 1024, &qmap, &q_full[qi & 1], 0, qrow + G);
+                } else {
+                    tma_load_2d(qb, &qmap, &q_full[qi & 1], 0, qrow);
+                    tma_load_2d(qb + 2048, &qmap, &q_full[qi & 1], 64, qrow);
+                }
             }
             __syncwarp();
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
@@ -941,16 +964,16 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             const bool first_piece = t == my_start;
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
-            float m_run[G], l_part[G], acc[G];
+            float m_run[GV], l_part[GV], acc[GV];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
+            for (int h = 0; h < GV; ++h) {
                 m_run[h] = -INFINITY;
                 l_part[h] = 0.f;
                 acc[h] = 0.f;
             }
             // O of tile jp (its PV used P relative to the max of tile jp) folds
             // into acc after the correction alpha of tile jp.
-            float alpha_prev[G];
+            float alpha_prev[GV];
             auto fold = [&](uint32_t jp) {
                 const uint32_t buf = jp & 1, par = (jp >> 1) & 1;
                 aborted = aborted ||
@@ -966,7 +989,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 }
                 mbar_arrive(&o_empty[buf]);
 #pragma unroll
-                for (int h = 0; h < G; ++h) acc[h] = acc[h] * alpha_prev[h] + (o[h] + o[LO + h]);
+                for (int h = 0; h < GV; ++h) acc[h] = acc[h] * alpha_prev[h] + (o[h] + o[LO + h]);
             };
             // Tile j's scores and P first, then the O of tile j - 1: the PV
             // round trip of one tile hides behind the softmax of the next.
@@ -986,18 +1009,19 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 mbar_arrive(&s_empty[buf]);
                 const int valid = min(kTcTile, L - k * kTcTile);
                 const bool live = row < valid;
-                float x[G];
+                float x[GV];
 #pragma unroll
-                for (int h = 0; h < G; ++h) {
-                    x[h] = live ? s[h] * a.scale_log2 : -INFINITY;
+                for (int h = 0; h < GV; ++h) {
+                    const int col = PAIR && h >= G ? 8 + h - G : h;  // S^T column of head h
+                    x[h] = live ? s[col] * a.scale_log2 : -INFINITY;
                     const float wm = warp_max(x[h]);
                     if (lane == 0) red[buf * 64 + q4 * 16 + h] = wm;
                 }
                 group_sync();
-                float alpha[G];
+                float alpha[GV];
                 unsigned char *pbuf = sm + kTcPOff + buf * kTcPBuf;
 #pragma unroll
-                for (int h = 0; h < G; ++h) {
+                for (int h = 0; h < GV; ++h) {
                     const float *rr = red + buf * 64 + h;
                     const float tmax = fmaxf(fmaxf(rr[0], rr[16]), fmaxf(rr[32], rr[48]));
                     const float m_new = fmaxf(m_run[h], tmax);
@@ -1026,31 +1050,37 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 mbar_arrive(&p_full[buf]);
                 if (k > P.k0) fold(j - 1);
 #pragma unroll
-                for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+                for (int h = 0; h < GV; ++h) alpha_prev[h] = alpha[h];
             }
             if (P.k1 > P.k0) fold(j - 1);
             // ---- finish the piece: l over the group, then output or partial ----
-            float l[G];
+            float l[GV];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
+            for (int h = 0; h < GV; ++h) {
                 const float ls = warp_sum(l_part[h]);
                 if (lane == 0) lred[q4 * 16 + h] = ls;
             }
             group_sync();
 #pragma unroll
-            for (int h = 0; h < G; ++h) l[h] = lred[h] + lred[16 + h] + lred[32 + h] + lred[48 + h];
+            for (int h = 0; h < GV; ++h) l[h] = lred[h] + lred[16 + h] + lred[32 + h] + lred[48 + h];
             group_sync();
-            OT *out = static_cast<OT *>(a.out) + ((int64_t)P.b * q_heads + (int64_t)P.g * G) * 128;
+            OT *out = static_cast<OT *>(a.out) + ((int64_t)P.b * q_heads + (int64_t)P.g * GV) * OD;
             if (P.k0 == 0 && P.k1 == P.nt) {  // the whole segment ran here
 #pragma unroll
-                for (int h = 0; h < G; ++h)
-                    out[h * 128 + row] = from_f32<OT>(l[h] > 0.f ? acc[h] / l[h] : 0.f);
+                for (int h = 0; h < GV; ++h) {
+                    const float v = l[h] > 0.f ? acc[h] / l[h] : 0.f;
+                    if constexpr (PAIR) {
+                        if ((h < G) == (row < 64)) out[h * 64 + (row & 63)] = from_f32<OT>(v);
+                    } else {
+                        out[h * 128 + row] = from_f32<OT>(v);
+                    }
+                }
                 continue;
             }
             const int kslot = first_piece ? 0 : 1;
             const int64_t slot = ((int64_t)blockIdx.x * 2 + kslot) * 16;
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
+            for (int h = 0; h < GV; ++h) {
                 a.part_o[(slot + h) * 128 + row] = acc[h];
                 if (wt == h) {
                     a.part_ml[(slot + h) * 2] = m_run[h];
@@ -1069,7 +1099,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             group_sync();
             if (*ticket) {
                 __threadfence();
-                merge_segment<OT>(a, 0, G, P.seg, P.nt, ncta, total_tiles, wt, 128, 1, mwst,
+                merge_segment<OT>(a, 0, GV, P.seg, P.nt, ncta, total_tiles, wt, 128, 1, mwst,
                                   mlst, mslot, nullptr, kInKernelMergeMax, out, group_sync);
                 if (wt == 0) a.counters[(int64_t)P.b * a.kv_heads + P.g] = 0u;
             }
@@ -1077,8 +1107,9 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         // empty sequences: no tile, zero output (the SDK's all-masked rule)
         for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
             if (__ldg(a.seq_lens + b) > 0) continue;
-            OT *ob = static_cast<OT *>(a.out) + (int64_t)b * q_heads * 128;
-            for (int h = 0; h < q_heads; ++h) ob[h * 128 + row] = from_f32<OT>(0.f);
+            OT *ob = static_cast<OT *>(a.out) + (int64_t)b * q_heads * OD;
+            if (row < OD)
+                for (int h = 0; h < q_heads; ++h) ob[h * OD + row] = from_f32<OT>(0.f);
         }
     }
     tc_fence_before();
@@ -1107,7 +1138,8 @@ pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     const int64_t seg = a.tile_prefix[b] + (int64_t)g * nt;
     if (cta_of_tile(seg, ncta, T) == cta_of_tile(seg + nt - 1, ncta, T)) return;
     OT *out = static_cast<OT *>(a.out) +
-              ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) * 128;
+              ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) *
+                  (a.pair_split != 0 ? 64 : 128);
     merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, 128, 4, wst, lst, slot, red,
                       kTcMaxGrid, out, [] { __syncthreads(); });
 }
@@ -1204,10 +1236,11 @@ bool encode_pool_map(CUtensorMap *map, const void *pool, uint64_t rows, uint64_t
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int G, typename T, typename OT>
+template <int G, typename T, typename OT, bool PAIR>
 int launch_tc(const TcArgs &args, const TcMaps &mp, int ncta,
               cudaStream_t stream) {
-    auto kern = paged_decode_tc_kernel<G, T, OT>;
+    auto kern = paged_decode_tc_kernel<G, T, OT, PAIR>;
+    constexpr int GV = PAIR ? 2 * G : G;  // query heads per segment
     static int configured[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1234,45 +1267,60 @@ int launch_tc(const TcArgs &args, const TcMaps &mp, int ncta,
     if (cudaLaunchKernelEx(&cfg, kern, args, mp.k, mp.v, mp.q) != cudaSuccess) return 0;
     if (!args.merge_in_kernel) {
         cudaLaunchConfig_t mc = cfg;
-        mc.gridDim = dim3(args.kv_heads * G, args.batch);
+        mc.gridDim = dim3(args.kv_heads * GV, args.batch);
         mc.blockDim = dim3(128);
         mc.dynamicSmemBytes = 0;
-        if (cudaLaunchKernelEx(&mc, pkv_tc_merge_kernel<OT>, args, G, ncta) != cudaSuccess)
+        if (cudaLaunchKernelEx(&mc, pkv_tc_merge_kernel<OT>, args, GV, ncta) != cudaSuccess)
             return 0;
     }
     return cudaGetLastError() == cudaSuccess;
 }
 
 template <typename T, typename OT>
-int dispatch_tc_group(const TcArgs &args, int group, const TcMaps &mp, int ncta, cudaStream_t s) {
+int dispatch_tc_group(const TcArgs &args, int group, bool pair, const TcMaps &mp, int ncta,
+                      cudaStream_t s) {
+    if (pair) {
+        switch (group) {
+            case 1: return launch_tc<1, T, OT, true>(args, mp, ncta, s);
+            case 2: return launch_tc<2, T, OT, true>(args, mp, ncta, s);
+            case 4: return launch_tc<4, T, OT, true>(args, mp, ncta, s);
+            case 8: return launch_tc<8, T, OT, true>(args, mp, ncta, s);
+            default: return 0;
+        }
+    }
     switch (group) {
-        case 1: return launch_tc<1, T, OT>(args, mp, ncta, s);
-        case 2: return launch_tc<2, T, OT>(args, mp, ncta, s);
-        case 4: return launch_tc<4, T, OT>(args, mp, ncta, s);
-        case 8: return launch_tc<8, T, OT>(args, mp, ncta, s);
-        case 16: return launch_tc<16, T, OT>(args, mp, ncta, s);
+        case 1: return launch_tc<1, T, OT, false>(args, mp, ncta, s);
+        case 2: return launch_tc<2, T, OT, false>(args, mp, ncta, s);
+        case 4: return launch_tc<4, T, OT, false>(args, mp, ncta, s);
+        case 8: return launch_tc<8, T, OT, false>(args, mp, ncta, s);
+        case 16: return launch_tc<16, T, OT, false>(args, mp, ncta, s);
         default: return 0;
     }
 }
 
-int dispatch_tc(const TcArgs &args, int group, bool bf16, PkvDType out, const TcMaps &mp,
-                int ncta, cudaStream_t s) {
+int dispatch_tc(const TcArgs &args, int group, bool pair, bool bf16, PkvDType out,
+                const TcMaps &mp, int ncta, cudaStream_t s) {
     if (!bf16)
         return out == PKV_DTYPE_F32
-                   ? dispatch_tc_group<__half, float>(args, group, mp, ncta, s)
-                   : dispatch_tc_group<__half, __half>(args, group, mp, ncta, s);
+                   ? dispatch_tc_group<__half, float>(args, group, pair, mp, ncta, s)
+                   : dispatch_tc_group<__half, __half>(args, group, pair, mp, ncta, s);
     return out == PKV_DTYPE_F32
-               ? dispatch_tc_group<__nv_bfloat16, float>(args, group, mp, ncta, s)
-               : dispatch_tc_group<__nv_bfloat16, __nv_bfloat16>(args, group, mp, ncta, s);
+               ? dispatch_tc_group<__nv_bfloat16, float>(args, group, pair, mp, ncta, s)
+               : dispatch_tc_group<__nv_bfloat16, __nv_bfloat16>(args, group, pair, mp, ncta, s);
 }
 
-bool tc_eligible(size_t head_dim, size_t block_size, size_t group, size_t rows) {
+// The tensor-core kernel takes head_dim 128 (GQA groups up to 16), and
+// head_dim 64 when the KV heads pair up (an even count, groups up to 8).
+bool tc_eligible(size_t head_dim, size_t kv_heads, size_t block_size, size_t group,
+                 size_t rows) {
     const char *force = getenv("PKV_DECODE_KERNEL");
     if (force != nullptr && strcmp(force, "simt") == 0) return false;
-    return head_dim == 128 && (block_size == 16 || block_size == 32 || block_size == 64 ||
-                               block_size == 128) &&
-           (group == 1 || group == 2 || group == 4 || group == 8 || group == 16) &&
-           rows < (size_t(1) << 31);
+    const bool pages = block_size == 16 || block_size == 32 || block_size == 64 ||
+                       block_size == 128;
+    const bool g128 = group == 1 || group == 2 || group == 4 || group == 8 || group == 16;
+    const bool g64 = (group == 1 || group == 2 || group == 4 || group == 8) && kv_heads % 2 == 0;
+    return pages && rows < (size_t(1) << 31) &&
+           ((head_dim == 128 && g128) || (head_dim == 64 && g64));
 }
 
 template <int HD, typename T>
@@ -1348,7 +1396,7 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         return 0;
     }
     const size_t group = q_heads / kvh;
-    const bool use_tc = pkv::tc_eligible(hd, layer->block_size, group,
+    const bool use_tc = pkv::tc_eligible(hd, kvh, layer->block_size, group,
                                          layer->block_count * layer->block_size);
     if (group != 1 && group != 2 && group != 4 && group != 8 && !(use_tc && group == 16)) {
         pkv_internal_set_error(error, error_capacity,
@@ -1430,7 +1478,11 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         t.part_o = reinterpret_cast<float *>(wsb + tws.o);
         t.tile_prefix = reinterpret_cast<int32_t *>(wsb + tws.prefix);
         t.table_stride = (int32_t)batch->table_stride;
-        t.kv_heads = (int32_t)kvh;
+        // head_dim 64: KV heads 2g and 2g+1 are one 128-column segment g
+        const bool pair = hd == 64;
+        const size_t segs = pair ? kvh / 2 : kvh;  // segments per sequence
+        t.kv_heads = (int32_t)segs;
+        t.pair_split = pair ? (int32_t)group : 0;
         t.block_size = (int32_t)layer->block_size;
         t.block_count = (uint32_t)layer->block_count;
         t.scale_log2 = scale * pkv::kLog2e;
@@ -1439,8 +1491,8 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         // CTA that finishes last, so with few segments (each cut into many
         // pieces, e.g. one long sequence) the separate merge kernel, one CTA
         // per query head, finishes sooner.
-        const bool fits = ncta / (int)kvh + 2 <= pkv::kInKernelMergeMax;
-        const bool many_segments = batch->batch * kvh * 2 >= (size_t)ncta;
+        const bool fits = ncta / (int)segs + 2 <= pkv::kInKernelMergeMax;
+        const bool many_segments = batch->batch * segs * 2 >= (size_t)ncta;
         t.merge_in_kernel = fits && many_segments;
         // launches of at most kTcMaxBatch sequences (their prefix lives in smem)
         const size_t osz = output_dtype == PKV_DTYPE_F32 ? 4 : 2;
@@ -1456,8 +1508,8 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
             sl.query = static_cast<const char *>(query) + b0 * q_heads * hd * 2;
             sl.q_row0 = (int32_t)(b0 * q_heads);
             sl.out = static_cast<char *>(output) + b0 * q_heads * hd * osz;
-            sl.counters = t.counters + b0 * kvh;
-            ok = pkv::dispatch_tc(sl, (int)group, bf16, output_dtype, mp, ncta, s);
+            sl.counters = t.counters + b0 * segs;
+            ok = pkv::dispatch_tc(sl, (int)group, pair, bf16, output_dtype, mp, ncta, s);
         }
     } else if (layer->dtype == PKV_DTYPE_F16)
         ok = hd == 128 ? pkv::dispatch_group<128, __half>(a, (int)group, output_dtype, s)
@@ -1598,7 +1650,8 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
     // anything above the array is refused.
     const size_t group = q_heads / kvh;
     size_t need;
-    if (pkv::tc_eligible(hd, layer->block_size, group, layer->block_count * layer->block_size)) {
+    if (pkv::tc_eligible(hd, kvh, layer->block_size, group,
+                         layer->block_count * layer->block_size)) {
         need = pkv::tc_workspace(batch->batch, kvh).total;
     } else {
         const size_t chunk = pkv::pick_chunk(0, max_seq_len);

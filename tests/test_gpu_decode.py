@@ -100,6 +100,37 @@ def test_tcgen05_shapes(lib, oracle_mod, cuda, group, block_size, dtype):
     assert P.device_fault(0) == 0
 
 
+@pytest.mark.parametrize("group,kv_heads,block_size,dtype", [
+    (1, 8, 16, "f16"),     # config 1's shape: MHA 8 heads, head_dim 64
+    (2, 2, 16, "bf16"), (4, 4, 32, "f16"), (8, 2, 16, "bf16"), (2, 6, 64, "f16")])
+def test_tcgen05_head_dim_64_paired(lib, oracle_mod, cuda, group, kv_heads, block_size, dtype):
+    """head_dim 64 on the tensor cores: KV heads 2g and 2g+1 run as one
+    128-column segment (block-diagonal query tile).  Ragged lengths, a
+    split over many CTAs, pages of 16-64 tokens, storage-dtype output."""
+    import torch
+    lengths = [0, 1, 15, 16, 17, 127, 128, 129, 700, 5000]
+    case = PagedCase(lengths, kv_heads * group, kv_heads, 64, block_size, dtype,
+                     seed=300 + 7 * group + kv_heads, device=cuda)
+    want = _oracle(case, oracle_mod)
+    got, _ = _run_decode(case, torch.float32)
+    check_close(got, want, f"d=64 paired group {group} kv {kv_heads} block {block_size}")
+    half, _ = _run_decode(case, case.d_q.dtype)
+    assert np.array_equal(half, _round_like(got, dtype)), "storage-dtype output rounding"
+    assert P.device_fault(0) == 0
+
+
+def test_tcgen05_head_dim_64_one_long_sequence(lib, oracle_mod, cuda):
+    """One long sequence at head_dim 64 with two KV heads: one segment cut
+    into a piece per CTA, merged by the separate merge kernel (paired
+    outputs of 64 dims)."""
+    import torch
+    case = PagedCase([40000, 3], 8, 2, 64, 16, "f16", seed=31, device=cuda)
+    want = _oracle(case, oracle_mod)
+    got, _ = _run_decode(case, torch.float32)
+    check_close(got, want, "d=64 wide split")
+    assert P.device_fault(0) == 0
+
+
 def test_wide_split_uses_merge_kernel(lib, oracle_mod, cuda):
     """One KV head and one long sequence: every CTA takes a piece of the same
     (sequence, head) segment, so the separate merge kernel combines ~148
@@ -122,13 +153,14 @@ def test_batch_above_one_launch(lib, oracle_mod, cuda):
     check_close(got, want, "1100 sequences")
 
 
-@pytest.mark.parametrize("group", [1, 4, 8])
-def test_simt_kernel_head_dim_128(lib, oracle_mod, cuda, monkeypatch, group):
-    """The CUDA-core kernel (forced) on the shapes the tcgen05 kernel serves."""
+@pytest.mark.parametrize("group,head_dim", [(1, 128), (4, 128), (8, 128), (2, 64), (4, 64)])
+def test_simt_kernel_forced(lib, oracle_mod, cuda, monkeypatch, group, head_dim):
+    """The CUDA-core kernel (forced) on shapes the tcgen05 kernel serves."""
     import torch
     monkeypatch.setenv("PKV_DECODE_KERNEL", "simt")
     lengths = [0, 1, 16, 17, 200, 777]
-    case = PagedCase(lengths, 2 * group, 2, 128, 16, "f16", seed=50 + group, device=cuda)
+    case = PagedCase(lengths, 2 * group, 2, head_dim, 16, "f16", seed=50 + group,
+                     device=cuda)
     want = _oracle(case, oracle_mod)
     for chunk in (0, 128):
         got, _ = _run_decode(case, torch.float32, chunk)

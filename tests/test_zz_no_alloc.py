@@ -58,11 +58,12 @@ def test_matches_workspace_entry_two_calls(lib, oracle_mod, cuda, q_heads, kv_he
 
 def test_refuses_shapes_above_the_static_maximum(lib, cuda):
     import torch
-    case = PagedCase([40], 8, 2, 64, 16, "f16", seed=5, device=cuda)
+    case = PagedCase([40], 8, 1, 64, 16, "f16", seed=5, device=cuda)
     out = torch.empty(1, 8, 64, dtype=torch.float32, device=cuda)
     err = ctypes.create_string_buffer(256)
-    # a CUDA-core shape (head_dim 64) declaring up to 16M positions: its
-    # per-chunk partials would need ~35 MB, above the 8 MiB array
+    # a CUDA-core shape (head_dim 64 with one KV head, which the tensor-core
+    # kernel does not pair) declaring up to 16M positions: its per-chunk
+    # partials would need ~35 MB, above the 8 MiB array
     ok = lib.pkv_paged_decode_static_scratch(ctypes.byref(case.layer()),
                                              ctypes.byref(case.batch()), 8, case.d_q.data_ptr(),
                                              ctypes.c_float(case.scale), out.data_ptr(),
