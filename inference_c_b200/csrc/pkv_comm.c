@@ -7,11 +7,15 @@
  * the return code and the rollback of the decode transaction
  * (src/common/attention.c:159-166).  Across GPUs a failure is a peer that
  * never joins or stops part-way, and a blocking NCCL call would then wait
- * forever.  This module therefore uses NCCL's non-blocking mode: init and
- * every enqueue return at once, and the host polls ncclCommGetAsyncError
- * (and the stream) against a deadline; past it, ncclCommAbort ends the
- * communicator's work (NCCL's kernels watch its abort flag) and the caller
- * gets 0 and rolls its step back.
+ * forever.  This module therefore joins in NCCL's non-blocking mode (init
+ * returns at once and the host polls ncclCommGetAsyncError against a
+ * deadline), then splits off a blocking child communicator for the
+ * collectives: a blocking enqueue only queues work (it never waits for
+ * peers) and is several times faster than a non-blocking one, whose enqueue
+ * completes asynchronously.  Waiting for a collective polls the stream and
+ * the child's error state against a deadline; past it, ncclCommAbort ends
+ * both communicators' work (NCCL's kernels watch the abort flag) and the
+ * caller gets 0 and rolls its step back.
  *
  * NCCL is loaded at run time (dlopen of PKV_NCCL_LIBRARY, default
  * libnccl.so.2 -- the one the process already has, e.g. torch's), so the
@@ -35,6 +39,7 @@
 typedef struct {
     ncclResult_t (*get_unique_id)(ncclUniqueId *);
     ncclResult_t (*init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
+    ncclResult_t (*split)(ncclComm_t, int, int, ncclComm_t *, ncclConfig_t *);
     ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t *);
     ncclResult_t (*abort)(ncclComm_t);
     ncclResult_t (*finalize)(ncclComm_t);
@@ -65,6 +70,7 @@ static void load_nccl(void) {
     }
     PKV_SYM(get_unique_id, "ncclGetUniqueId")
     PKV_SYM(init_rank_config, "ncclCommInitRankConfig")
+    PKV_SYM(split, "ncclCommSplit")
     PKV_SYM(get_async_error, "ncclCommGetAsyncError")
     PKV_SYM(abort, "ncclCommAbort")
     PKV_SYM(finalize, "ncclCommFinalize")
@@ -82,7 +88,8 @@ static int nccl_ready(char *error, size_t cap, const char *what) {
 }
 
 struct PkvComm {
-    ncclComm_t comm;
+    ncclComm_t parent;  /* non-blocking: joins under a deadline */
+    ncclComm_t comm;    /* blocking child of `parent`: the collectives */
     int device, nranks, rank;
     int aborted;
     /* completion check of the enqueued work: NULL = cudaStreamQuery(stream);
@@ -97,26 +104,32 @@ static double now_s(void) {
     return (double)t.tv_sec + 1e-9 * (double)t.tv_nsec;
 }
 
-static void nap(void) {
-    const struct timespec t = {0, 50000}; /* 50 us between polls */
+/* Between polls: spin for the first 2 ms of a wait (an enqueue or a small
+ * collective settles in microseconds, and the device may be idle until the
+ * host sees it), then sleep 20 us per poll. */
+static void nap(double started) {
+    if (now_s() - started < 2e-3) return;
+    const struct timespec t = {0, 20000};
     nanosleep(&t, NULL);
 }
 
 static void abort_comm(PkvComm *c) {
     if (!c->aborted) {
-        (void)g_nccl.abort(c->comm);
+        if (c->comm != NULL) (void)g_nccl.abort(c->comm);
+        if (c->parent != NULL) (void)g_nccl.abort(c->parent);
         c->aborted = 1;
     }
 }
 
-/* Polls the communicator until its pending operation (init or an enqueue)
- * leaves ncclInProgress, or until `deadline`; on timeout or error the
- * communicator is aborted.  1 on success. */
-static int settle(PkvComm *c, double deadline, char *error, size_t cap, const char *what,
-                  const char *waiting_for) {
+/* Polls communicator `h` until its pending operation (init, split or an
+ * enqueue) leaves ncclInProgress, or until `deadline`; on timeout or error
+ * the communicators are aborted.  1 on success. */
+static int settle(PkvComm *c, ncclComm_t h, double deadline, char *error, size_t cap,
+                  const char *what, const char *waiting_for) {
+    const double started = now_s();
     for (;;) {
         ncclResult_t state = ncclInProgress;
-        const ncclResult_t r = g_nccl.get_async_error(c->comm, &state);
+        const ncclResult_t r = g_nccl.get_async_error(h, &state);
         if (r != ncclSuccess) state = r;
         if (state == ncclSuccess) return 1;
         if (state != ncclInProgress) {
@@ -131,7 +144,7 @@ static int settle(PkvComm *c, double deadline, char *error, size_t cap, const ch
                                    waiting_for);
             return 0;
         }
-        nap();
+        nap(started);
     }
 }
 
@@ -183,16 +196,28 @@ int pkv_comm_init(const unsigned char *id, size_t id_bytes, int nranks, int rank
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0; /* every call returns at once; completion is polled */
     const double deadline = now_s() + timeout_s;
-    const ncclResult_t r = g_nccl.init_rank_config(&c->comm, nranks, u, rank, &cfg);
+    ncclResult_t r = g_nccl.init_rank_config(&c->parent, nranks, u, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) {
         pkv_internal_set_error(error, cap, "%s: %s", what, g_nccl.error_string(r));
-        if (c->comm != NULL) abort_comm(c);
+        if (c->parent != NULL) abort_comm(c);
         goto done;
     }
     char waiting[96];
     snprintf(waiting, sizeof waiting, "after %.3g s waiting for the %d other rank(s) to join",
              timeout_s, nranks - 1);
-    if (!settle(c, deadline, error, cap, what, waiting)) goto done;
+    if (!settle(c, c->parent, deadline, error, cap, what, waiting)) goto done;
+    /* the blocking child for the collectives (the split itself runs in the
+     * parent's non-blocking mode, under the same deadline) */
+    ncclConfig_t child_cfg = NCCL_CONFIG_INITIALIZER;
+    child_cfg.blocking = 1;
+    r = g_nccl.split(c->parent, 0, rank, &c->comm, &child_cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        abort_comm(c);
+        pkv_internal_set_error(error, cap, "%s: split: %s", what, g_nccl.error_string(r));
+        goto done;
+    }
+    if (!settle(c, c->comm, deadline, error, cap, what, "splitting the collective communicator"))
+        goto done;
     *comm = c;
     c = NULL;
     ok = 1;
@@ -225,7 +250,7 @@ int pkv_comm_all_gather(PkvComm *comm, const void *send, void *recv, size_t byte
                                g_nccl.error_string(r));
         ok = 0;
     } else {
-        ok = settle(comm, deadline, error, cap, what, "enqueueing the all-gather");
+        ok = settle(comm, comm->comm, deadline, error, cap, what, "enqueueing the all-gather");
     }
     PKV_RANGE_POP();
     return ok;
@@ -242,7 +267,7 @@ int pkv_comm_wait(PkvComm *comm, PkvStream stream, double timeout_s, char *error
         return 0;
     }
     PKV_RANGE_PUSH(what);
-    const double deadline = now_s() + timeout_s;
+    const double started = now_s(), deadline = started + timeout_s;
     int ok = 0;
     for (;;) {
         ncclResult_t state = ncclSuccess;
@@ -280,7 +305,7 @@ int pkv_comm_wait(PkvComm *comm, PkvStream stream, double timeout_s, char *error
                                    what, timeout_s);
             break;
         }
-        nap();
+        nap(started);
     }
     PKV_RANGE_POP();
     return ok;
@@ -294,17 +319,21 @@ void pkv_comm_destroy(PkvComm *comm) {
         int prev = 0;
         const int have_prev = cudaGetDevice(&prev) == cudaSuccess;
         if (comm->device >= 0) cudaSetDevice(comm->device);
-        /* non-blocking teardown: finalize (flushes outstanding work), wait a
-         * bounded time for it, then free; a finalize that does not settle
-         * aborts the communicator instead */
-        const ncclResult_t r = g_nccl.finalize(comm->comm);
-        const int settled =
+        /* finalize flushes outstanding work: the blocking child returns when
+         * done, the non-blocking parent is polled a bounded time; whatever
+         * does not settle is aborted instead of freed */
+        const int child_done = g_nccl.finalize(comm->comm) == ncclSuccess;
+        const ncclResult_t r = child_done ? g_nccl.finalize(comm->parent) : ncclInternalError;
+        const int parent_done =
             (r == ncclSuccess || r == ncclInProgress) &&
-            settle(comm, now_s() + 10.0, NULL, 0, "pkv_comm_destroy", "finalizing");
-        if (settled)
+            settle(comm, comm->parent, now_s() + 10.0, NULL, 0, "pkv_comm_destroy",
+                   "finalizing");
+        if (child_done && parent_done) {
             (void)g_nccl.destroy(comm->comm);
-        else
+            (void)g_nccl.destroy(comm->parent);
+        } else {
             abort_comm(comm);
+        }
         if (have_prev) cudaSetDevice(prev);
     }
     free(comm);

@@ -82,8 +82,8 @@ def test_all_ranks_join_and_collective_completes(lib, tmp_path):
         lib.pkv_comm_destroy(h)
     """, _env(tmp_path, so))
     log = (tmp_path / "log").read_text().splitlines()
-    assert log == ["init nonblocking rank 0", "allgather rank 0", "finalize rank 0",
-                   "destroy rank 0"]
+    assert log == ["init nonblocking rank 0", "split blocking rank 0", "allgather rank 0",
+                   "finalize rank 0", "finalize rank 0", "destroy rank 0", "destroy rank 0"]
 
 
 WORKER = """
@@ -173,7 +173,8 @@ def test_stalled_collective_is_abandoned_at_the_deadline(lib, tmp_path):
     """, _env(tmp_path, so))
     assert "ok" in out
     log = (tmp_path / "log").read_text().splitlines()
-    assert log.count("abort rank 0") == 1 and "destroy rank 0" not in log
+    # both communicators (the joining parent and the collectives' child) aborted
+    assert log.count("abort rank 0") == 2 and "destroy rank 0" not in log
 
 
 def test_refuses_bad_arguments(lib):
