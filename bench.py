@@ -26,6 +26,7 @@ Run under torchrun for N > 1 (RANK/LOCAL_RANK/WORLD_SIZE from the env).
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import datetime
 import json
 import math
@@ -60,6 +61,10 @@ def parse_args():
                    help="wall-time budget of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--head-dim", type=int, choices=[64, 128], default=0,
+                   help="configs 2/3 only: run the configuration with this head size instead "
+                        "of its 128 (64 takes the paired tensor-core decode); a variant, not a "
+                        "BASELINE.json configuration, and named so in config.workload")
     p.add_argument("--comm", choices=["pkv", "torch"], default="pkv",
                    help="config 4 all-gather: the library's NCCL communicator with a host "
                         "deadline (pkv_comm_*), or torch.distributed's all_gather_into_tensor")
@@ -94,8 +99,18 @@ def metric_name(cfg: int) -> str:
             "SDPA per step)" % cfg)
 
 
-def config_block(cfg: int, n: int, chunk: int) -> dict:
+def decode_config(cfg: int, head_dim: int = 0):
+    """The workload of a decode configuration, optionally at another head
+    size (a variant: the name says so)."""
     c = W.CONFIGS[cfg]
+    if head_dim and head_dim != c.head_dim:
+        c = dataclasses.replace(c, head_dim=head_dim,
+                                name=f"{c.name} -- variant at head_dim {head_dim}")
+    return c
+
+
+def config_block(cfg: int, n: int, chunk: int, head_dim: int = 0) -> dict:
+    c = decode_config(cfg, head_dim)
     d = {"workload": c.name, "batch": c.batch, "q_heads": c.q_heads, "kv_heads": c.kv_heads,
          "head_dim": c.head_dim, "block_size": c.block_size, "storage": "f16",
          "accumulate": "f32", "decode_chunk_tokens": chunk,
@@ -293,7 +308,7 @@ def run_ours(args) -> None:
                                 device_id=dev)
     P.load()
     cfg = args.config
-    c = W.CONFIGS[cfg]
+    c = decode_config(cfg, args.head_dim)
     if cfg == 3:
         all_len = W.context_lengths(3, args.seed)
         shard = W.shard_by_length(all_len, world)[rank]
@@ -485,7 +500,7 @@ def run_ours(args) -> None:
     alg_bytes = dec_bytes
     peak, peak_kind = peak_hbm()
     achieved = alg_bytes / (mean_dec / 1e3) / 1e9
-    ratio = traffic_ratio(cfg)
+    ratio = traffic_ratio(cfg) if c.head_dim == 128 else None  # captured at head_dim 128
     per_rank = {"rank": rank, "decode_ms": mean_dec, "gbs": achieved, "seqs": n,
                 "tokens": int(cur.sum())}
     gathered = [per_rank]
@@ -511,7 +526,7 @@ def run_ours(args) -> None:
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic: seeded N(0,1) FP16 Q/K/V on the device, seeded lengths",
-            "config": config_block(cfg, world, chunk),
+            "config": config_block(cfg, world, chunk, args.head_dim),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": None if ratio is None else ratio * alg_bytes,
