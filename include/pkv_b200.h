@@ -123,7 +123,9 @@ int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes,
  * stream cut evenly across the CTAs (stream-K); a segment split between CTAs
  * is merged from FP32 partials (m, l, O) by the last CTA to finish it, or,
  * when few segments are cut into many pieces, by a separate merge kernel.
- * head_dim 64 (and other page sizes) run a CUDA-core kernel: one CTA per
+ * head_dim 64 with an even KV-head count runs there too, KV heads 2g and
+ * 2g+1 as one 128-column segment.  Other shapes (head_dim 64 with an odd
+ * KV-head count, other page sizes) run a CUDA-core kernel: one CTA per
  * (sequence, KV head, chunk of chunk_tokens positions), a cp.async ring and
  * a warp-shuffle online softmax, chunks merged by the last CTA.
  * max_seq_len bounds seq_lens (it sizes the scratch); chunk_tokens 0 picks a
@@ -240,8 +242,9 @@ int pkv_sdpa_f16_host(const uint16_t *query, const uint16_t *key,
  * the step back.  NCCL is loaded at run time (PKV_NCCL_LIBRARY, default
  * libnccl.so.2). */
 typedef struct PkvComm PkvComm;
-#define PKV_COMM_ID_BYTES 128
-/* A new communicator id (rank 0 makes it and sends it to the others). */
+#define PKV_COMM_ID_BYTES 256
+/* A new communicator id (rank 0 makes it and sends it to the others; it
+ * holds two NCCL ids: the joining and the collectives' communicator). */
 int pkv_comm_unique_id(unsigned char *id, size_t id_bytes, char *error, size_t error_capacity);
 /* Joins the communicator of `id` as `rank` of `nranks` on `device`; waits at
  * most timeout_s seconds for every rank to join. */

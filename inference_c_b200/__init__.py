@@ -547,7 +547,7 @@ def sdpa_f16_host(query, key, value, scale: float, causal: bool, mask=None):
 # NCCL all-gather with a host deadline (multi-GPU head split)
 # ---------------------------------------------------------------------------
 
-COMM_ID_BYTES = 128
+COMM_ID_BYTES = 256
 
 
 def comm_unique_id() -> bytes:
@@ -564,7 +564,7 @@ class Comm:
     def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int,
                  timeout_s: float):
         if len(unique_id) != COMM_ID_BYTES:
-            raise ValueError("unique id must be 128 bytes")
+            raise ValueError(f"unique id must be {COMM_ID_BYTES} bytes")
         self._id = ctypes.create_string_buffer(unique_id, COMM_ID_BYTES)
         h = _c_ptr()
         _call("pkv_comm_init", self._id, COMM_ID_BYTES, nranks, rank, device,

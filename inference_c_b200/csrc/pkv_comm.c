@@ -7,15 +7,17 @@
  * the return code and the rollback of the decode transaction
  * (src/common/attention.c:159-166).  Across GPUs a failure is a peer that
  * never joins or stops part-way, and a blocking NCCL call would then wait
- * forever.  This module therefore joins in NCCL's non-blocking mode (init
- * returns at once and the host polls ncclCommGetAsyncError against a
- * deadline), then splits off a blocking child communicator for the
- * collectives: a blocking enqueue only queues work (it never waits for
- * peers) and is several times faster than a non-blocking one, whose enqueue
- * completes asynchronously.  Waiting for a collective polls the stream and
- * the child's error state against a deadline; past it, ncclCommAbort ends
- * both communicators' work (NCCL's kernels watch the abort flag) and the
- * caller gets 0 and rolls its step back.
+ * forever.  This module therefore joins a communicator in NCCL's
+ * non-blocking mode first (init returns at once and the host polls
+ * ncclCommGetAsyncError against a deadline): that proves every rank is
+ * alive.  The collectives then run on a second, blocking communicator
+ * (initialised from its own id, in a helper thread, under the same
+ * deadline): a blocking enqueue only queues work -- it never waits for
+ * peers -- and is several times faster than a non-blocking one, whose
+ * enqueue completes asynchronously.  Waiting for a collective polls the
+ * stream and the communicator's error state against a deadline; past it,
+ * ncclCommAbort ends both communicators' work (NCCL's kernels watch the
+ * abort flag) and the caller gets 0 and rolls its step back.
  *
  * NCCL is loaded at run time (dlopen of PKV_NCCL_LIBRARY, default
  * libnccl.so.2 -- the one the process already has, e.g. torch's), so the
@@ -39,7 +41,6 @@
 typedef struct {
     ncclResult_t (*get_unique_id)(ncclUniqueId *);
     ncclResult_t (*init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
-    ncclResult_t (*split)(ncclComm_t, int, int, ncclComm_t *, ncclConfig_t *);
     ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t *);
     ncclResult_t (*abort)(ncclComm_t);
     ncclResult_t (*finalize)(ncclComm_t);
@@ -70,7 +71,6 @@ static void load_nccl(void) {
     }
     PKV_SYM(get_unique_id, "ncclGetUniqueId")
     PKV_SYM(init_rank_config, "ncclCommInitRankConfig")
-    PKV_SYM(split, "ncclCommSplit")
     PKV_SYM(get_async_error, "ncclCommGetAsyncError")
     PKV_SYM(abort, "ncclCommAbort")
     PKV_SYM(finalize, "ncclCommFinalize")
@@ -89,7 +89,7 @@ static int nccl_ready(char *error, size_t cap, const char *what) {
 
 struct PkvComm {
     ncclComm_t parent;  /* non-blocking: joins under a deadline */
-    ncclComm_t comm;    /* blocking child of `parent`: the collectives */
+    ncclComm_t comm;    /* blocking: the collectives */
     int device, nranks, rank;
     int aborted;
     /* completion check of the enqueued work: NULL = cudaStreamQuery(stream);
@@ -148,6 +148,72 @@ static int settle(PkvComm *c, ncclComm_t h, double deadline, char *error, size_t
     }
 }
 
+typedef struct {
+    PkvComm *c;
+    ncclUniqueId id;
+    ncclResult_t result;
+    int done;  /* set (atomically) when the init returned */
+} BlockingInit;
+
+static void *blocking_init_main(void *arg) {
+    BlockingInit *job = (BlockingInit *)arg;
+    PkvComm *c = job->c;
+    if (c->device >= 0) cudaSetDevice(c->device); /* NCCL binds the current device */
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 1;
+    job->result = g_nccl.init_rank_config(&c->comm, c->nranks, job->id, c->rank, &cfg);
+    __atomic_store_n(&job->done, 1, __ATOMIC_RELEASE);
+    return NULL;
+}
+
+/* Initialises c->comm (blocking mode) from `id` before `deadline`.  On
+ * timeout the joining communicator is aborted, the helper thread is left
+ * inside NCCL (it owns `c` and the job from then on) and 0 is returned; on
+ * any other failure `c` is freed. */
+static int init_blocking(PkvComm *c, const unsigned char *id, double deadline, char *error,
+                         size_t cap, const char *what) {
+    BlockingInit *job = (BlockingInit *)calloc(1, sizeof *job);
+    if (job == NULL) {
+        abort_comm(c);
+        pkv_internal_set_error(error, cap, "%s: out of host memory", what);
+        free(c);
+        return 0;
+    }
+    job->c = c;
+    memcpy(job->id.internal, id, NCCL_UNIQUE_ID_BYTES);
+    pthread_t tid;
+    if (pthread_create(&tid, NULL, blocking_init_main, job) != 0) {
+        abort_comm(c);
+        pkv_internal_set_error(error, cap, "%s: cannot start the init thread", what);
+        free(job);
+        free(c);
+        return 0;
+    }
+    const double started = now_s();
+    while (!__atomic_load_n(&job->done, __ATOMIC_ACQUIRE)) {
+        if (now_s() > deadline) {
+            pthread_detach(tid);
+            if (c->parent != NULL) (void)g_nccl.abort(c->parent);
+            pkv_internal_set_error(error, cap,
+                                   "%s: timed out initialising the collective communicator "
+                                   "(a rank stopped after joining); joining communicator "
+                                   "aborted", what);
+            return 0;
+        }
+        nap(started);
+    }
+    pthread_join(tid, NULL);
+    const ncclResult_t r = job->result;
+    free(job);
+    if (r != ncclSuccess) {
+        abort_comm(c);
+        pkv_internal_set_error(error, cap, "%s: %s", what, g_nccl.error_string(r));
+        free(c);
+        return 0;
+    }
+    return 1;
+}
+
 int pkv_comm_unique_id(unsigned char *id, size_t id_bytes, char *error, size_t cap) {
     const char *what = "pkv_comm_unique_id";
     if (id == NULL || id_bytes != PKV_COMM_ID_BYTES) {
@@ -156,13 +222,15 @@ int pkv_comm_unique_id(unsigned char *id, size_t id_bytes, char *error, size_t c
         return 0;
     }
     if (!nccl_ready(error, cap, what)) return 0;
-    ncclUniqueId u;
-    const ncclResult_t r = g_nccl.get_unique_id(&u);
-    if (r != ncclSuccess) {
-        pkv_internal_set_error(error, cap, "%s: %s", what, g_nccl.error_string(r));
-        return 0;
+    for (int k = 0; k < 2; ++k) {  /* the joining and the collectives' communicator */
+        ncclUniqueId u;
+        const ncclResult_t r = g_nccl.get_unique_id(&u);
+        if (r != ncclSuccess) {
+            pkv_internal_set_error(error, cap, "%s: %s", what, g_nccl.error_string(r));
+            return 0;
+        }
+        memcpy(id + k * NCCL_UNIQUE_ID_BYTES, u.internal, NCCL_UNIQUE_ID_BYTES);
     }
-    memcpy(id, u.internal, PKV_COMM_ID_BYTES);
     return 1;
 }
 
@@ -192,7 +260,7 @@ int pkv_comm_init(const unsigned char *id, size_t id_bytes, int nranks, int rank
         goto done;
     }
     ncclUniqueId u;
-    memcpy(u.internal, id, PKV_COMM_ID_BYTES);
+    memcpy(u.internal, id, NCCL_UNIQUE_ID_BYTES);
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0; /* every call returns at once; completion is polled */
     const double deadline = now_s() + timeout_s;
@@ -206,18 +274,13 @@ int pkv_comm_init(const unsigned char *id, size_t id_bytes, int nranks, int rank
     snprintf(waiting, sizeof waiting, "after %.3g s waiting for the %d other rank(s) to join",
              timeout_s, nranks - 1);
     if (!settle(c, c->parent, deadline, error, cap, what, waiting)) goto done;
-    /* the blocking child for the collectives (the split itself runs in the
-     * parent's non-blocking mode, under the same deadline) */
-    ncclConfig_t child_cfg = NCCL_CONFIG_INITIALIZER;
-    child_cfg.blocking = 1;
-    r = g_nccl.split(c->parent, 0, rank, &c->comm, &child_cfg);
-    if (r != ncclSuccess && r != ncclInProgress) {
-        abort_comm(c);
-        pkv_internal_set_error(error, cap, "%s: split: %s", what, g_nccl.error_string(r));
+    /* the collectives' blocking communicator, initialised in a helper thread
+     * (a blocking init returns only when every rank joined) under the same
+     * deadline; all ranks were seen alive a moment ago */
+    if (!init_blocking(c, id + NCCL_UNIQUE_ID_BYTES, deadline, error, cap, what)) {
+        c = NULL;  /* owned by the helper thread if it is still inside NCCL */
         goto done;
     }
-    if (!settle(c, c->comm, deadline, error, cap, what, "splitting the collective communicator"))
-        goto done;
     *comm = c;
     c = NULL;
     ok = 1;
@@ -322,7 +385,7 @@ void pkv_comm_destroy(PkvComm *comm) {
         /* finalize flushes outstanding work: the blocking child returns when
          * done, the non-blocking parent is polled a bounded time; whatever
          * does not settle is aborted instead of freed */
-        const int child_done = g_nccl.finalize(comm->comm) == ncclSuccess;
+        const int child_done = g_nccl.finalize(comm->comm) == ncclSuccess;  /* blocking */
         const ncclResult_t r = child_done ? g_nccl.finalize(comm->parent) : ncclInternalError;
         const int parent_done =
             (r == ncclSuccess || r == ncclInProgress) &&

@@ -62,26 +62,6 @@ ncclResult_t ncclCommInitRankConfig(ncclComm_t *comm, int nranks, ncclUniqueId i
     return c->blocking ? ncclSuccess : ncclInProgress;
 }
 
-/* A child joins once every rank split (its own marker files); the call is
- * non-blocking when the parent is, whatever the child's own mode. */
-ncclResult_t ncclCommSplit(ncclComm_t comm, int color, int key, ncclComm_t *newcomm,
-                           ncclConfig_t *config) {
-    (void)color; (void)key;
-    struct ncclComm *c = calloc(1, sizeof *c);
-    if (c == NULL) return ncclSystemError;
-    c->nranks = comm->nranks;
-    c->rank = comm->rank;
-    c->blocking = !(config != NULL && config->blocking == 0);
-    snprintf(c->name, sizeof c->name, "%.40ss", comm->name);
-    char path[512];
-    snprintf(path, sizeof path, "%s/%s.%d", dir_of(), c->name, c->rank);
-    FILE *f = fopen(path, "w");
-    if (f != NULL) fclose(f);
-    log_line(c->blocking ? "split blocking" : "split nonblocking", c->rank);
-    *newcomm = c;
-    return comm->blocking ? ncclSuccess : ncclInProgress;
-}
-
 ncclResult_t ncclCommGetAsyncError(ncclComm_t comm, ncclResult_t *state) {
     int joined = 0;
     for (int r = 0; r < comm->nranks; ++r) {

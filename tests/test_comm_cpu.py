@@ -30,15 +30,15 @@ PRELUDE = textwrap.dedent(r"""
 
     def init(uid, nranks, rank, timeout):
         h = ctypes.c_void_p()
-        buf = ctypes.create_string_buffer(uid, 128)
+        buf = ctypes.create_string_buffer(uid, 256)
         t0 = time.monotonic()
-        ok = lib.pkv_comm_init(buf, 128, nranks, rank, -1, ctypes.c_double(timeout),
+        ok = lib.pkv_comm_init(buf, 256, nranks, rank, -1, ctypes.c_double(timeout),
                                ctypes.byref(h), err, len(err))
         return ok, h.value, time.monotonic() - t0
 
     def uid():
-        buf = ctypes.create_string_buffer(128)
-        assert lib.pkv_comm_unique_id(buf, 128, err, len(err)) == 1, err.value
+        buf = ctypes.create_string_buffer(256)
+        assert lib.pkv_comm_unique_id(buf, 256, err, len(err)) == 1, err.value
         return buf.raw
 """)
 
@@ -82,7 +82,7 @@ def test_all_ranks_join_and_collective_completes(lib, tmp_path):
         lib.pkv_comm_destroy(h)
     """, _env(tmp_path, so))
     log = (tmp_path / "log").read_text().splitlines()
-    assert log == ["init nonblocking rank 0", "split blocking rank 0", "allgather rank 0",
+    assert log == ["init nonblocking rank 0", "init blocking rank 0", "allgather rank 0",
                    "finalize rank 0", "finalize rank 0", "destroy rank 0", "destroy rank 0"]
 
 
@@ -173,7 +173,7 @@ def test_stalled_collective_is_abandoned_at_the_deadline(lib, tmp_path):
     """, _env(tmp_path, so))
     assert "ok" in out
     log = (tmp_path / "log").read_text().splitlines()
-    # both communicators (the joining parent and the collectives' child) aborted
+    # both communicators (the joining one and the collectives' one) aborted
     assert log.count("abort rank 0") == 2 and "destroy rank 0" not in log
 
 
@@ -181,8 +181,8 @@ def test_refuses_bad_arguments(lib):
     import ctypes
     err = ctypes.create_string_buffer(256)
     h = ctypes.c_void_p()
-    assert lib.pkv_comm_init(None, 128, 2, 0, -1, ctypes.c_double(1.0), ctypes.byref(h), err,
+    assert lib.pkv_comm_init(None, 256, 2, 0, -1, ctypes.c_double(1.0), ctypes.byref(h), err,
                              len(err)) == 0
-    assert lib.pkv_comm_unique_id(None, 128, err, len(err)) == 0
+    assert lib.pkv_comm_unique_id(None, 256, err, len(err)) == 0
     assert lib.pkv_comm_wait(None, None, ctypes.c_double(1.0), err, len(err)) == 0
     assert lib.pkv_comm_aborted(None) == 1
