@@ -65,9 +65,11 @@ def parse_args():
                    help="configs 2/3 only: run the configuration with this head size instead "
                         "of its 128 (64 takes the paired tensor-core decode); a variant, not a "
                         "BASELINE.json configuration, and named so in config.workload")
-    p.add_argument("--comm", choices=["pkv", "torch"], default="pkv",
+    p.add_argument("--comm", choices=["pkv", "torch", "peer"], default="pkv",
                    help="config 4 all-gather: the library's NCCL communicator with a host "
-                        "deadline (pkv_comm_*), or torch.distributed's all_gather_into_tensor")
+                        "deadline (pkv_comm_*), torch.distributed's all_gather_into_tensor "
+                        "(NCCL), or the library's peer-store all-gather over NVLink "
+                        "(pkv_peer_*, an A/B variant)")
     p.add_argument("--prefill-batch", type=int, default=0,
                    help="config 5 only: sequences per step (default: the config's 8; smaller "
                         "values make small cases for profiling)")
@@ -758,7 +760,13 @@ def run_cfg4(args) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     P.load()
-    comm = None
+    comm = peer = None
+    if dist is not None and args.comm == "peer":
+        nbytes = (c.kv_heads // world) * (c.q_heads // c.kv_heads) * c.head_dim * 2
+        peer = P.PeerGather(local, world, rank, nbytes)
+        handles = [None] * world
+        dist.all_gather_object(handles, peer.ipc_handle)
+        peer.connect(handles)
     if dist is not None and args.comm == "pkv":
         # the library's non-blocking NCCL communicator: a peer that never joins
         # or stalls ends the wait at the deadline (and the step rolls back)
@@ -824,6 +832,8 @@ def run_cfg4(args) -> None:
         dst = full if full_out is None else full_out
         if comm is not None:
             comm.all_gather(out, dst, stream, timeout_s=10.0)  # per-head outputs, NVLink
+        elif peer is not None:
+            peer.all_gather(out, dst, stream, timeout_s=5.0)
         elif dist is not None:
             dist.all_gather_into_tensor(dst, out)
         else:
@@ -846,6 +856,8 @@ def run_cfg4(args) -> None:
     def gather_only():
         if comm is not None:
             comm.all_gather(out, full, stream, timeout_s=10.0)
+        elif peer is not None:
+            peer.all_gather(out, full, stream, timeout_s=5.0)
         else:
             dist.all_gather_into_tensor(full, out)
 
@@ -952,7 +964,9 @@ def run_cfg4(args) -> None:
             "config": {"workload": c.name, "tokens": L0, "q_heads": c.q_heads,
                        "kv_heads": c.kv_heads, "head_dim": c.head_dim, "block_size": 16,
                        "kv_heads_per_gpu": kvl,
-                       "parallelism": f"KV-head split over {world} GPU(s) + NCCL all-gather",
+                       "parallelism": (f"KV-head split over {world} GPU(s) + "
+                                       + ("peer-store all-gather" if peer is not None
+                                          else "NCCL all-gather")),
                        "l2": "no flush needed: 512 MiB of pages per step at one GPU"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                          "frac": gbs / peak, "traffic": None, "peak_kind": peak_kind,
@@ -961,14 +975,17 @@ def run_cfg4(args) -> None:
             "allgather_ms": ag,
             "allgather_timing": "the all-gather alone, each call after a barrier and "
                                 "synchronize (latency without rank skew)",
-            "allgather_api": ("pkv_comm_all_gather (non-blocking NCCL communicator, host "
-                              "deadline)" if comm is not None else
+            "allgather_api": ("pkv_comm_all_gather (NCCL, joined under a host deadline)"
+                              if comm is not None else
+                              "pkv_peer_all_gather (peer stores over NVLink, bounded waits)"
+                              if peer is not None else
                               "torch.distributed all_gather_into_tensor (NCCL)"),
             "cpu_baseline": None,
             "e2e": {"value": 1.0 / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": (h_q.numel() + h_k.numel() + h_v.numel()) * 2 * world,
                     "d2h_bytes_per_step": h_o.numel() * 2},
-            "gpu_launches": steps * 4,  # staging, append, decode, merge (+ NCCL's kernel)
+            "gpu_launches": steps * (4 + (peer is not None)),  # staging, append, decode,
+                                                                 # merge (+ gather / NCCL's)
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -976,6 +993,10 @@ def run_cfg4(args) -> None:
     if comm is not None:
         comm.wait(stream, timeout_s=60.0)
         comm.destroy()
+    if peer is not None:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still stores into another's area
+        peer.destroy()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -264,6 +264,28 @@ int pkv_comm_wait(PkvComm *comm, PkvStream stream, double timeout_s, char *error
 int pkv_comm_aborted(const PkvComm *comm);
 void pkv_comm_destroy(PkvComm *comm);
 
+/* All-gather by peer stores over NVLink (an A/B alternative to the NCCL
+ * all-gather above for small per-rank outputs; no counterpart in the SDK).
+ * Each rank allocates a device area, exports it with CUDA IPC (the handle,
+ * PKV_PEER_HANDLE_BYTES), and maps every other rank's.  One single-CTA
+ * kernel per call stores this rank's bytes into every rank's area and waits
+ * (bounded by timeout_s, on the GPU) until every rank's bytes of this step
+ * arrived, then copies the nranks slots (rank order) to recv.  A wait that
+ * gives up records fault code 4 (pkv_device_fault) and leaves recv as it
+ * was.  All ranks must call it the same number of times, on GPUs of one
+ * node with peer access.  Up to 8 ranks and 1 MiB per rank. */
+typedef struct PkvPeerGather PkvPeerGather;
+#define PKV_PEER_HANDLE_BYTES 64
+int pkv_peer_gather_create(int device, int nranks, int rank, size_t bytes_per_rank,
+                           PkvPeerGather **gather, void *handle, size_t handle_bytes,
+                           char *error, size_t error_capacity);
+/* handles: every rank's handle, rank order (nranks * PKV_PEER_HANDLE_BYTES). */
+int pkv_peer_gather_connect(PkvPeerGather *gather, const void *handles, size_t handles_bytes,
+                            char *error, size_t error_capacity);
+int pkv_peer_all_gather(PkvPeerGather *gather, const void *send, void *recv, double timeout_s,
+                        PkvStream stream, char *error, size_t error_capacity);
+void pkv_peer_gather_destroy(PkvPeerGather *gather);
+
 /* ---------------------------------------------------------------------- */
 /* 2. Host transaction layer                                               */
 /* ---------------------------------------------------------------------- */

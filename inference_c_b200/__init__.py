@@ -168,6 +168,12 @@ EXPORTS = {
     "pkv_comm_wait": (_c_int, [_c_ptr, _c_ptr, ctypes.c_double, *_ERR]),
     "pkv_comm_aborted": (_c_int, [_c_ptr]),
     "pkv_comm_destroy": (None, [_c_ptr]),
+    # include/pkv_b200.h -- all-gather by peer stores
+    "pkv_peer_gather_create": (_c_int, [_c_int, _c_int, _c_int, _c_size, ctypes.POINTER(_c_ptr),
+                                        _c_ptr, _c_size, *_ERR]),
+    "pkv_peer_gather_connect": (_c_int, [_c_ptr, _c_ptr, _c_size, *_ERR]),
+    "pkv_peer_all_gather": (_c_int, [_c_ptr, _c_ptr, _c_ptr, ctypes.c_double, _c_ptr, *_ERR]),
+    "pkv_peer_gather_destroy": (None, [_c_ptr]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -587,4 +593,35 @@ class Comm:
     def destroy(self) -> None:
         if self.handle:
             load().pkv_comm_destroy(self.handle)
+            self.handle = None
+
+
+PEER_HANDLE_BYTES = 64
+
+
+class PeerGather:
+    """pkv_peer_gather_*: all-gather of `nbytes` per rank by peer stores over
+    NVLink.  Create on every rank, exchange `handle` (bytes), then connect
+    with all ranks' handles in rank order."""
+
+    def __init__(self, device: int, nranks: int, rank: int, nbytes: int):
+        h = _c_ptr()
+        buf = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+        _call("pkv_peer_gather_create", device, nranks, rank, nbytes, ctypes.byref(h), buf,
+              PEER_HANDLE_BYTES)
+        self.handle = h.value
+        self.ipc_handle = buf.raw
+
+    def connect(self, handles: list) -> None:
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _call("pkv_peer_gather_connect", self.handle, buf, len(blob))
+
+    def all_gather(self, send, recv, stream=None, timeout_s: float = 1.0) -> None:
+        _call("pkv_peer_all_gather", self.handle, send.data_ptr(), recv.data_ptr(),
+              ctypes.c_double(timeout_s), _stream_ptr(stream))
+
+    def destroy(self) -> None:
+        if self.handle:
+            load().pkv_peer_gather_destroy(self.handle)
             self.handle = None

@@ -22,7 +22,8 @@ LIBDIR = HERE / "lib"
 LIBRARY = LIBDIR / "libpkv_b200.so"
 
 C_SOURCES = ["paged_kv_cache.c", "pkv_pool.c", "pkv_comm.c"]
-CU_SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_sequence.cu", "pkv_dense.cu"]
+CU_SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_sequence.cu", "pkv_dense.cu",
+              "pkv_peer.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

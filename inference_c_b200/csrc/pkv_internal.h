@@ -49,6 +49,13 @@ int pkv_internal_take_copy_fault(uint32_t *code);
 int pkv_internal_take_decode_fault(uint32_t *code);
 int pkv_internal_take_prefill_fault(uint32_t *code);
 int pkv_internal_take_sequence_fault(uint32_t *code);
+int pkv_internal_take_peer_fault(uint32_t *code);
+
+/* Tests on one GPU: makes `area` (a device buffer of
+ * pkv_internal_peer_gather_area_bytes bytes on this GPU) stand in for the
+ * area of `rank`, so a peer that never stores can be simulated. */
+int pkv_internal_peer_gather_set_area(PkvPeerGather *gather, int rank, void *area);
+size_t pkv_internal_peer_gather_area_bytes(const PkvPeerGather *gather);
 
 /* Writes `code` into the prefill fault word of the current device: a
  * host-side stand-in for a kernel that recorded a fault, so tests can check

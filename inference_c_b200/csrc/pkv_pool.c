@@ -441,16 +441,16 @@ int pkv_device_fault(int device, uint32_t *code, char *error, size_t cap) {
     const int have_prev = cudaGetDevice(&prev) == cudaSuccess;
     cudaError_t st = cudaSetDevice(device);
     if (st == cudaSuccess) st = cudaDeviceSynchronize();
-    uint32_t a = 0, b = 0, c = 0, d = 0;
+    uint32_t a = 0, b = 0, c = 0, d = 0, e = 0;
     int ok = st == cudaSuccess && pkv_internal_take_copy_fault(&a) &&
              pkv_internal_take_decode_fault(&b) && pkv_internal_take_prefill_fault(&c) &&
-             pkv_internal_take_sequence_fault(&d);
+             pkv_internal_take_sequence_fault(&d) && pkv_internal_take_peer_fault(&e);
     if (have_prev) cudaSetDevice(prev);
     if (!ok) {
         pkv_internal_set_error(error, cap, "pkv_device_fault: %s",
                                cudaGetErrorString(st != cudaSuccess ? st : cudaGetLastError()));
         return 0;
     }
-    *code = a ? a : (b ? b : (c ? c : d));
+    *code = a ? a : (b ? b : (c ? c : (d ? d : e)));
     return 1;
 }
