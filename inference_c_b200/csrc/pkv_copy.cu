@@ -103,20 +103,25 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
 // One step's staging, read straight from the pinned host slot (no copy on
 // the stream): the lengths and row offsets go to the device slot the kernels
 // of the step read, the new page-table entries into the padded table.  One
-// CTA; when it is done it writes `ticket` to the slot's host word, which
-// tells the host the slot may be refilled.
+// CTA for a decode step; a large staging (a prefix import: thousands of new
+// entries) spreads over several, which count themselves out on `arrive`
+// (a device word, zero between launches).  The last CTA to finish writes
+// `ticket` to the slot's host word, which tells the host the slot may be
+// refilled.
 __global__ void __launch_bounds__(512)
 stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ dev_lens,
                    int batch, int max_batch, const PkvTablePatch *__restrict__ host_patches,
                    int64_t count, uint32_t *__restrict__ table, int64_t stride, int64_t rows,
-                   volatile uint32_t *host_done, uint32_t ticket) {
+                   uint32_t *arrive, volatile uint32_t *host_done, uint32_t ticket) {
     pdl_launch_dependents();
     pdl_wait();  // the previous step's kernels no longer read the table or this slot
-    for (int i = threadIdx.x; i <= batch; i += blockDim.x) {
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = first; i <= batch; i += step) {
         if (i < batch) dev_lens[i] = host_lens[i];
         dev_lens[max_batch + i] = host_lens[max_batch + i];
     }
-    for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+    for (int64_t i = first; i < count; i += step) {
         const PkvTablePatch p = host_patches[i];
         if ((int64_t)p.row >= rows || (int64_t)p.index >= stride) {
             record_fault(&g_copy_fault, kFaultPositionOutOfRange);
@@ -124,10 +129,14 @@ stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ 
         }
         table[(int64_t)p.row * stride + p.index] = p.page;
     }
-    __syncthreads();  // every read of the host slot has returned
+    __syncthreads();  // every read of the host slot by this CTA has returned
     if (threadIdx.x == 0) {
-        __threadfence_system();
-        *host_done = ticket;
+        __threadfence();
+        if (atomicAdd(arrive, 1u) == gridDim.x - 1) {  // the last CTA
+            *arrive = 0u;
+            __threadfence_system();
+            *host_done = ticket;
+        }
     }
 }
 
@@ -261,12 +270,19 @@ int pkv_kv_gather(const PkvPagedLayer *layer, const PkvBatch *batch, const int32
 int pkv_internal_stage_apply(const int32_t *host_lens, int32_t *dev_lens, size_t batch,
                              size_t max_batch, const PkvTablePatch *host_patches, size_t count,
                              uint32_t *table, size_t table_stride, size_t table_rows,
-                             uint32_t *host_done, uint32_t ticket, PkvStream stream) {
+                             uint32_t *arrive, uint32_t *host_done, uint32_t ticket,
+                             PkvStream stream) {
     const unsigned threads = count > 256 || batch > 256 ? 512u : 256u;
+    const size_t work = count > batch ? count : batch;
+    const size_t per_cta = 4096;  // bus reads in flight per CTA, roughly
+    const unsigned grid = (unsigned)(work <= per_cta ? 1 : (work + per_cta - 1) / per_cta < 64
+                                                                ? (work + per_cta - 1) / per_cta
+                                                                : 64);
     const cudaError_t st = pkv::launch_pdl(
-        pkv::stage_apply_kernel, dim3(1), dim3(threads), (cudaStream_t)stream, host_lens,
+        pkv::stage_apply_kernel, dim3(grid), dim3(threads), (cudaStream_t)stream, host_lens,
         dev_lens, (int)batch, (int)max_batch, host_patches, (int64_t)count, table,
-        (int64_t)table_stride, (int64_t)table_rows, (volatile uint32_t *)host_done, ticket);
+        (int64_t)table_stride, (int64_t)table_rows, arrive, (volatile uint32_t *)host_done,
+        ticket);
     return st == cudaSuccess && cudaGetLastError() == cudaSuccess;
 }
 

@@ -28,11 +28,14 @@ typedef struct {
  * and host_done): lengths [batch] and row offsets [batch+1] (laid out at
  * host_lens and host_lens + max_batch) go to dev_lens (same layout), `count`
  * patches into the padded device table; then `ticket` is written to
- * *host_done, after which the host may refill the slot. */
+ * *host_done, after which the host may refill the slot.  `arrive` is a
+ * device word, zero before the launch (the kernel leaves it zero), that the
+ * kernel's CTAs count themselves out on. */
 int pkv_internal_stage_apply(const int32_t *host_lens, int32_t *dev_lens, size_t batch,
                              size_t max_batch, const PkvTablePatch *host_patches, size_t count,
                              uint32_t *table, size_t table_stride, size_t table_rows,
-                             uint32_t *host_done, uint32_t ticket, PkvStream stream);
+                             uint32_t *arrive, uint32_t *host_done, uint32_t ticket,
+                             PkvStream stream);
 
 /* Copies page ids [from, page_count) of `sequence` into dst and reports the
  * full page count; 0 for an unknown handle or a too-small capacity.  One

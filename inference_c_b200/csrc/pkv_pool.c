@@ -178,8 +178,10 @@ int pkv_pool_create(TensorPagedKVCache *cache, int device, PkvDType dtype,
         st = cudaHostAlloc((void **)&p->h_stage[s], p->stage_bytes, map_flags);
         if (st == cudaSuccess)
             st = cudaHostGetDevicePointer((void **)&p->h_stage_dev[s], p->h_stage[s], 0);
+        /* lengths and offsets, then the staging kernel's arrival counter */
         if (st == cudaSuccess)
-            st = cudaMalloc((void **)&p->d_stage[s], p->patch_offset);
+            st = cudaMalloc((void **)&p->d_stage[s], p->patch_offset + 256);
+        if (st == cudaSuccess) st = cudaMemset(p->d_stage[s], 0, p->patch_offset + 256);
     }
     if (st == cudaSuccess)
         st = cudaHostAlloc((void **)&p->h_consumed, kStageSlots * sizeof(uint32_t), map_flags);
@@ -362,6 +364,7 @@ static int step_begin_impl(PkvPool *pool, const TensorPagedKVSequence *sequences
                                   (int32_t *)p->d_stage[slot], batch, p->max_batch,
                                   (const PkvTablePatch *)(p->h_stage_dev[slot] + p->patch_offset),
                                   npatch, p->d_tables, p->max_pages, p->max_batch,
+                                  (uint32_t *)(p->d_stage[slot] + p->patch_offset),
                                   p->h_consumed_dev + slot, ticket, stream))
         st = cudaErrorLaunchFailure;
     else
