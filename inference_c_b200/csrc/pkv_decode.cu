@@ -1119,16 +1119,18 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
 }
 
 // Merges segments that span more than kInKernelMergeMax CTAs.  Grid:
-// (kv_heads * G, batch), one query head per CTA; 128 threads, four per output
-// float4 (each summing every fourth piece).
+// (kv_heads * G, batch), one query head per CTA; kMergeThreads threads,
+// sixteen per output float4 (each summing every sixteenth piece), so the
+// ~150 partial rows of a segment cut across every SM load in one round.
+constexpr int kMergeThreads = 512;
 template <typename OT>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kMergeThreads)
 pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     pdl_wait();
     __shared__ float wst[kTcMaxGrid];
     __shared__ float lst[kTcMaxGrid];
     __shared__ int slot[kTcMaxGrid];
-    __shared__ float4 red[128];
+    __shared__ float4 red[kMergeThreads];
     const int b = blockIdx.y;
     const int g = blockIdx.x / group, h = blockIdx.x - g * group;
     const int64_t T = a.tile_prefix[a.batch];
@@ -1140,8 +1142,8 @@ pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     OT *out = static_cast<OT *>(a.out) +
               ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) *
                   (a.pair_split != 0 ? 64 : 128);
-    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, 128, 4, wst, lst, slot, red,
-                      kTcMaxGrid, out, [] { __syncthreads(); });
+    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, kMergeThreads, kMergeThreads / 32,
+                      wst, lst, slot, red, kTcMaxGrid, out, [] { __syncthreads(); });
 }
 
 int g_sm_count[64];
@@ -1268,7 +1270,7 @@ int launch_tc(const TcArgs &args, const TcMaps &mp, int ncta,
     if (!args.merge_in_kernel) {
         cudaLaunchConfig_t mc = cfg;
         mc.gridDim = dim3(args.kv_heads * GV, args.batch);
-        mc.blockDim = dim3(128);
+        mc.blockDim = dim3(kMergeThreads);
         mc.dynamicSmemBytes = 0;
         if (cudaLaunchKernelEx(&mc, pkv_tc_merge_kernel<OT>, args, GV, ncta) != cudaSuccess)
             return 0;
