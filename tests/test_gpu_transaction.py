@@ -186,3 +186,48 @@ def test_truncation_resends_table_rows(lib, oracle_mod, cuda):
     pool.step_end(True)
     assert P.device_fault(0) == 0
     cache.free()
+
+
+def test_large_staging_spreads_over_ctas(lib, cuda):
+    """A step that brings 5,600 new page-table entries (a prefix import of
+    many pages) is applied by several staging CTAs: the rows imported through
+    it must read back bit for bit through the table, and so must the rows of
+    the two small steps after it (one staging CTA, both slots reused)."""
+    import torch
+    n, per = 8, 700  # 8 sequences x 700 pages of 16 tokens
+    cache = P.PagedKVCache(16, n * (per + 2), n)
+    pool = P.PagedPool(cache, 0, P.PKV_DTYPE_F16, 1, 1, 128, n, per + 2)
+    layer = pool.layer(0)
+    seqs = [cache.sequence_create() for _ in range(n)]
+    lengths = np.array([16 * per - 3 * b for b in range(n)], np.int64)
+    g = torch.Generator(device=cuda).manual_seed(11)
+    rows_k = [torch.randn(int(L), 128, generator=g, device=cuda).half() for L in lengths]
+    rows_v = [torch.randn(int(L), 128, generator=g, device=cuda).half() for L in lengths]
+
+    def offsets(counts):
+        return torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).to(cuda)
+
+    pool.step_begin(seqs, lengths.tolist())
+    P.kv_import(layer, pool.step_batch(), torch.cat(rows_k), torch.cat(rows_v), offsets(lengths))
+    pool.step_end(True)
+    for _ in range(2):  # one appended row per sequence per step
+        nk = torch.randn(n, 128, generator=g, device=cuda).half()
+        nv = torch.randn(n, 128, generator=g, device=cuda).half()
+        pool.step_begin(seqs, [1] * n)
+        P.kv_append(layer, pool.step_batch(), nk, nv)
+        pool.step_end(True)
+        for b in range(n):
+            rows_k[b] = torch.cat([rows_k[b], nk[b:b + 1]])
+            rows_v[b] = torch.cat([rows_v[b], nv[b:b + 1]])
+    lengths = lengths + 2
+    assert [cache.length(s_) for s_ in seqs] == lengths.tolist()
+    pool.step_begin(seqs, [0] * n)  # read everything back through the table
+    k = torch.empty(int(lengths.sum()), 128, dtype=torch.float16, device=cuda)
+    v = torch.empty_like(k)
+    P.kv_gather(layer, pool.step_batch(), k, v, offsets(lengths))
+    torch.cuda.synchronize()
+    pool.step_end(True)
+    assert np.array_equal(to_host_bits(k), to_host_bits(torch.cat(rows_k)))
+    assert np.array_equal(to_host_bits(v), to_host_bits(torch.cat(rows_v)))
+    assert P.device_fault(0) == 0
+    cache.free()
