@@ -62,9 +62,10 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--head-dim", type=int, choices=[64, 128], default=0,
-                   help="configs 2/3 only: run the configuration with this head size instead "
-                        "of its 128 (64 takes the paired tensor-core decode); a variant, not a "
-                        "BASELINE.json configuration, and named so in config.workload")
+                   help="configs 2, 3 and 7: run the configuration with this head size "
+                        "instead of its 128 (decode: 64 takes the paired tensor-core path); a "
+                        "variant, not a BASELINE.json configuration, named so in "
+                        "config.workload")
     p.add_argument("--comm", choices=["pkv", "torch", "peer"], default="pkv",
                    help="config 4 all-gather: the library's NCCL communicator with a host "
                         "deadline (pkv_comm_*), torch.distributed's all_gather_into_tensor "
@@ -1151,8 +1152,7 @@ def run_decoder(args) -> None:
 CFG7 = dict(batch=1, q_heads=32, kv_heads=8, q_len=4096, kv_len=4096, head_dim=128, causal=True)
 
 
-def cfg7_flops() -> float:
-    c = CFG7
+def cfg7_flops(c=CFG7) -> float:
     off = c["kv_len"] - c["q_len"]
     keys = sum(min(c["kv_len"], off + i + 1) for i in range(c["q_len"]))
     return 4.0 * c["head_dim"] * c["batch"] * c["q_heads"] * keys
@@ -1163,21 +1163,25 @@ def run_dense(args) -> None:
     if rank != 0:
         return
     import torch
-    c = CFG7
+    c = dict(CFG7)
+    if args.head_dim:
+        c["head_dim"] = args.head_dim
+    d = c["head_dim"]
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(args.seed)
     B, Hq, Hkv, Lq, Lk = c["batch"], c["q_heads"], c["kv_heads"], c["q_len"], c["kv_len"]
-    q = torch.randn(B, Hq, Lq, 128, generator=g, device=dev).half()
-    k = torch.randn(B, Hkv, Lk, 128, generator=g, device=dev).half()
-    v = torch.randn(B, Hkv, Lk, 128, generator=g, device=dev).half()
+    q = torch.randn(B, Hq, Lq, d, generator=g, device=dev).half()
+    k = torch.randn(B, Hkv, Lk, d, generator=g, device=dev).half()
+    v = torch.randn(B, Hkv, Lk, d, generator=g, device=dev).half()
     out = torch.empty_like(q)
-    scale = 1 / math.sqrt(128)
-    flops = cfg7_flops()
+    scale = 1 / math.sqrt(d)
+    flops = cfg7_flops(c)
     peak, kind = measured_peak_tflops()
     steps, warmup = args.steps, args.warmup
-    block = {"workload": "cfg7: dense causal FP16 SDPA, B=1, GQA 32/8, 4096 x 4096, d=128 "
-                         "(tensor_sdpa_f16's backend)", **c}
+    block = {"workload": f"cfg7: dense causal FP16 SDPA, B=1, GQA 32/8, 4096 x 4096, d={d} "
+                         "(tensor_sdpa_f16's backend)"
+                         + ("" if d == 128 else " -- variant at head_dim 64"), **c}
     sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid))
     h_q, h_k, h_v = (t.cpu().numpy().view(np.uint16) for t in (q, k, v))
     if args.impl == "reference":
