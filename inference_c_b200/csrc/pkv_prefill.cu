@@ -656,10 +656,11 @@ paged_prefill_tc_kernel(const PfArgs a, const __grid_constant__ CUtensorMap qmap
                 const float2 sc2 = make_float2(sc, sc);
                 // GEN: a row that has seen only -inf keeps m = -inf (use 0: its
                 // P is 0); one whose max is +inf is dead (P = 0, output 0)
-                float nm = -m_run;
+                // a row that has seen only masked keys so far keeps m = -inf:
+                // use 0 (its P is 0) rather than produce NaN from -inf + inf
+                float nm = m_run == -INFINITY ? 0.f : -m_run;
                 if constexpr (GEN) {
                     dead = dead || m_run == INFINITY;
-                    nm = m_run == -INFINITY ? 0.f : nm;
                     if (dead) {
 #pragma unroll
                         for (int c = 0; c < 4; ++c)
