@@ -1025,9 +1025,9 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                     const float *rr = red + buf * 64 + h;
                     const float tmax = fmaxf(fmaxf(rr[0], rr[16]), fmaxf(rr[32], rr[48]));
                     const float m_new = fmaxf(m_run[h], tmax);
-                    alpha[h] = exp2f(m_run[h] - m_new);
+                    alpha[h] = ex2_fast(m_run[h] - m_new);
                     m_run[h] = m_new;
-                    const float p = exp2f(x[h] - m_new);
+                    const float p = ex2_fast(x[h] - m_new);
                     const T hi = from_f32<T>(p);
                     const T lo = from_f32<T>(p - static_cast<float>(hi));
                     l_part[h] = l_part[h] * alpha[h] + p;
