@@ -370,24 +370,24 @@ def run_ours(args) -> None:
     max_len = int(lengths.max()) + grow
     ws = P.decode_workspace(n, c.q_heads, c.head_dim, max_len, chunk, device=dev)
     stream = torch.cuda.current_stream()
-    ones = [1] * n
     cur = lengths.copy()
     launches = {"n": 0}
     bytes_log: list[float] = []
     kv_bytes_per_token = c.kv_width * 2 * 2
 
-    def step(i: int | None, q_in=None, k_in=None, v_in=None, o_out=None):
+    stepper = P.DecodeStepper(pool, layer, seqs, q, newk, newv, out, c.scale, max_len, ws, chunk,
+                              stream)
+
+    def step(i: int | None, bufs=None):
         """One SDK transaction for the shard: step_begin (one staging kernel),
-        append, paged decode, step_end.  Nothing else is put on the stream
-        between the kernels, so each one's launch and prologue overlap the
-        one before it (programmatic dependent launch)."""
+        append, paged decode, step_end, through the C ABI with the arguments
+        bound once (DecodeStepper).  Nothing else is put on the stream between
+        the kernels, so each one's launch and prologue overlap the one before
+        it (programmatic dependent launch)."""
         nonlocal cur
-        pool.step_begin(seqs, ones)
-        b = pool.step_batch()
-        P.kv_append(layer, b, newk if k_in is None else k_in, newv if v_in is None else v_in)
-        P.paged_decode(layer, b, q if q_in is None else q_in, out if o_out is None else o_out,
-                       c.scale, max_len, ws, chunk)
-        pool.step_end(True)
+        if bufs is not None:
+            stepper.bind(*bufs)
+        stepper.step()
         cur = cur + 1
         if i is not None:
             launches["n"] += 3  # staging, append, decode
@@ -471,7 +471,7 @@ def run_ours(args) -> None:
                     if i + 1 < k:
                         upload(s_ ^ 1)
                     stream.wait_event(up_done[s_])
-                    step(None, d_q[s_], d_k[s_], d_v[s_], d_o[s_])
+                    step(None, (d_q[s_], d_k[s_], d_v[s_], d_o[s_]))
                     step_done[s_].record(stream)
                     used[s_] = True
                     with torch.cuda.stream(copy):
@@ -493,8 +493,9 @@ def run_ours(args) -> None:
             e2e = {"value": total_seqs / (e2e_ms / 1e3), "unit": "tokens/s",
                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
                    "d2h_bytes_per_step": d2h * world,
-                   "api": "pkv_step_begin/pkv_kv_append/pkv_paged_decode/pkv_step_end + "
-                          "pinned host<->device copies on a second stream, double-buffered"}
+                   "api": "pkv_step_begin/pkv_kv_append/pkv_paged_decode/pkv_step_end "
+                          "(DecodeStepper) + pinned host<->device copies on a second stream, "
+                          "double-buffered"}
     fault = P.device_fault(local)
     if fault:
         raise SystemExit(f"device fault code {fault} recorded during the bench")
@@ -820,15 +821,17 @@ def run_cfg4(args) -> None:
     stream = torch.cuda.current_stream()
     cur = [L0]
 
+    stepper = P.DecodeStepper(pool, layer, [seq], q, newk, newv, out, c.scale, max_len, ws, 0,
+                              stream)
+
     def step(q_in=None, k_in=None, v_in=None, full_out=None):
-        """Transaction, append, decode of this rank's heads, then the NCCL
-        all-gather of every rank's head outputs.  No events between the
-        kernels, so their launches overlap (programmatic dependent launch)."""
-        pool.step_begin([seq], [1])
-        b = pool.step_batch()
-        P.kv_append(layer, b, newk if k_in is None else k_in, newv if v_in is None else v_in)
-        P.paged_decode(layer, b, q if q_in is None else q_in, out, c.scale, max_len, ws)
-        pool.step_end(True)
+        """Transaction, append, decode of this rank's heads (DecodeStepper:
+        the C calls with their arguments bound once), then the all-gather of
+        every rank's head outputs.  No events between the kernels, so their
+        launches overlap (programmatic dependent launch)."""
+        if q_in is not None:
+            stepper.bind(q_in, k_in, v_in, out)
+        stepper.step()
         cur[0] += 1
         dst = full if full_out is None else full_out
         if comm is not None:

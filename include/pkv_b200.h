@@ -131,6 +131,11 @@ int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes,
  * max_seq_len bounds seq_lens (it sizes the scratch); chunk_tokens 0 picks a
  * split from batch and max_seq_len (the tensor-core kernel ignores it).
  * seq_lens[b] == 0 yields zeros, like the SDK's all-masked softmax.
+ * The tensor-core kernel releases programmatic dependents early: a kernel
+ * the caller launches after it on the same stream WITH programmatic stream
+ * serialization starts while it runs and must execute griddepcontrol.wait
+ * (cudaGridDependencySynchronize) before it reads the output or writes the
+ * pages or tables.  Ordinary launches, copies and events wait for it as usual.
  * Replaces decode_score_kernel, decode_softmax_kernel and
  * decode_attention_output_kernel (attention_cuda.cu:343-398, launched
  * :1001-1011). */

@@ -443,6 +443,70 @@ class PagedPool:
         _call("pkv_step_end", self.handle, int(commit))
 
 
+class DecodeStepper:
+    """One decode step of a fixed batch -- pkv_step_begin (one new token per
+    sequence), pkv_kv_append, pkv_paged_decode, pkv_step_end -- with every
+    argument converted once.  A step of a short batch runs for tens of
+    microseconds on the GPU; building the ctypes arguments, stream and dtype
+    lookups of the one-call wrappers again for each of the four calls would
+    make the Python host, not the GPU, set the step rate.  A failed call
+    rolls the open step back (pkv_step_end(0)) and raises."""
+
+    def __init__(self, pool: PagedPool, layer: PkvPagedLayer, sequences: Sequence[int], query,
+                 key_rows, value_rows, output, scale: float, max_seq_len: int, workspace,
+                 chunk_tokens: int = 0, stream=None):
+        lib = load()
+        n = len(sequences)
+        self._lib = lib
+        self._pool = pool.handle
+        self._n = n
+        self._seqs = (_c_u64 * n)(*sequences)
+        self._new = (_c_size * n)(*([1] * n))
+        self._stream = _stream_ptr(stream)
+        self._err = ctypes.create_string_buffer(512)
+        self._layer = layer
+        self._layer_ref = ctypes.byref(layer)
+        self._batch = PkvBatch()
+        self._batch_ref = ctypes.byref(self._batch)
+        self._q_heads = query.shape[-2]
+        self._scale = ctypes.c_float(scale)
+        self._out_dtype = _dtype_code(output)
+        self._max_len = max_seq_len
+        self._chunk = chunk_tokens
+        self._ws = workspace.data_ptr()
+        self._ws_bytes = workspace.numel()
+        self.bind(query, key_rows, value_rows, output)
+
+    def bind(self, query, key_rows, value_rows, output) -> None:
+        """Device buffers of the next steps (same shapes and dtypes)."""
+        if key_rows.shape[0] != self._n or value_rows.shape[0] != self._n:
+            raise ValueError("one new K and V row per sequence")
+        self._q, self._k, self._v = query.data_ptr(), key_rows.data_ptr(), value_rows.data_ptr()
+        self._o = output.data_ptr()
+
+    def _fail(self, name: str, opened: bool):
+        msg = self._err.value.decode(errors="replace")
+        if opened:
+            self._lib.pkv_step_end(self._pool, 0, self._err, 512)
+        raise PkvError(f"{name}: {msg}")
+
+    def step(self) -> None:
+        lib, err = self._lib, self._err
+        if not lib.pkv_step_begin(self._pool, self._seqs, None, self._new, self._n, self._stream,
+                                  err, 512):
+            self._fail("pkv_step_begin", False)
+        lib.pkv_step_batch(self._pool, self._batch_ref)
+        if not lib.pkv_kv_append(self._layer_ref, self._batch_ref, None, self._k, self._v, self._n,
+                                 self._stream, err, 512):
+            self._fail("pkv_kv_append", True)
+        if not lib.pkv_paged_decode(self._layer_ref, self._batch_ref, self._q_heads, self._q,
+                                    self._scale, self._o, self._out_dtype, self._max_len,
+                                    self._chunk, self._ws, self._ws_bytes, self._stream, err, 512):
+            self._fail("pkv_paged_decode", True)
+        if not lib.pkv_step_end(self._pool, 1, err, 512):
+            self._fail("pkv_step_end", False)
+
+
 # ---------------------------------------------------------------------------
 # include/attention.h: the SDK's paged decoder (greedy tokens of one sequence)
 # ---------------------------------------------------------------------------

@@ -114,15 +114,24 @@ stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ 
                    int64_t count, uint32_t *__restrict__ table, int64_t stride, int64_t rows,
                    uint32_t *arrive, volatile uint32_t *host_done, uint32_t ticket) {
     pdl_launch_dependents();
-    pdl_wait();  // the previous step's kernels no longer read the table or this slot
     const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    // Each thread's first items cross the bus while the kernels before this
+    // one drain (the decode kernel releases its dependents early): the host
+    // slot stays the host's, unchanged, until the ticket below, and no kernel
+    // writes it.  Nothing the earlier kernels read is written before the wait.
+    int32_t len0 = 0, off0 = 0;
+    PkvTablePatch p0 = {};
+    if (first < batch) len0 = host_lens[first];
+    if (first <= batch) off0 = host_lens[max_batch + first];
+    if (first < count) p0 = host_patches[first];
+    pdl_wait();  // the previous step's kernels no longer read the table or this slot
     for (int64_t i = first; i <= batch; i += step) {
-        if (i < batch) dev_lens[i] = host_lens[i];
-        dev_lens[max_batch + i] = host_lens[max_batch + i];
+        if (i < batch) dev_lens[i] = i == first ? len0 : host_lens[i];
+        dev_lens[max_batch + i] = i == first ? off0 : host_lens[max_batch + i];
     }
     for (int64_t i = first; i < count; i += step) {
-        const PkvTablePatch p = host_patches[i];
+        const PkvTablePatch p = i == first ? p0 : host_patches[i];
         if ((int64_t)p.row >= rows || (int64_t)p.index >= stride) {
             record_fault(&g_copy_fault, kFaultPositionOutOfRange);
             continue;

@@ -453,15 +453,22 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 // FP16 P costs ~1% relative error on small outputs).
 //
 // Work split ("stream-K"): the 128-token tiles of every (sequence, KV head)
-// segment, sequence-major, form one stream of T tiles and CTA i of n takes
-// tiles [T*i/n, T*(i+1)/n), so every CTA streams the same number of bytes
-// whatever the length mix.  A segment inside one CTA's range is finished
-// there; a segment cut by range ends leaves one partial (m, l, O) per piece,
-// in slot 0 (the CTA's first piece) or slot 1 (its last piece).  The last CTA
-// to finish a piece of such a segment merges them (atomic ticket), unless one
-// segment can span more than kInKernelMergeMax CTAs (few KV heads, one long
-// sequence); then pkv_tc_merge_kernel, one CTA per (sequence, query head),
-// merges after the decode kernel.
+// segment, sequence-major, form one stream of T tiles, cut into work units of
+// consecutive tiles.  Static units: unit i < n (one per CTA) is tiles
+// [S*i/n, S*(i+1)/n) of the static region [0, S), so every CTA streams the
+// same number of bytes whatever the length mix.  SMs do not stream at the same
+// rate (a few percent apart, differently in every launch), so with the
+// dynamic tail the last T - S tiles form rounds of n units each, unit sizes
+// halving from about an eighth of a CTA's share, and a CTA that finishes its
+// static unit claims the next unit with one atomic: the CTAs then finish
+// within about one small unit of one another instead of spreading over the
+// rate differences.  A segment inside one unit is finished there; a segment
+// cut by unit ends leaves one partial (m, l, O) per piece, in slot 0 (the
+// unit's first piece) or slot 1 (its last piece).  The last CTA to finish a
+// piece of such a segment merges them (atomic ticket), unless one segment can
+// span more than kInKernelMergeMax units (few KV heads, one long sequence);
+// then there is no dynamic tail and pkv_tc_merge_kernel, one CTA per
+// (sequence, query head), merges after the decode kernel.
 // ---------------------------------------------------------------------------
 constexpr int kTcThreads = 224;
 constexpr int kTcTile = 128;
@@ -469,13 +476,17 @@ constexpr int kTcStages = 3;
 constexpr int kTcMaxBatch = 1024;
 constexpr int kTcMaxGrid = 256;
 constexpr int kInKernelMergeMax = 32;
+constexpr int kMaxRounds = 5;                               // dynamic rounds
+constexpr int kTcMaxUnits = kTcMaxGrid * (1 + kMaxRounds);  // work units of one launch
+constexpr int kRing = 4;  // unit ids in flight from the K producer to the other roles
+constexpr size_t kMinUnitTiles = 8;  // smallest dynamic unit
 constexpr uint32_t kTcStageBytes = 65536;
 constexpr uint32_t kTcHalf = 16384;       // 128 rows x 128 bytes
 constexpr uint32_t kTcQOff = kTcStages * kTcStageBytes;
 constexpr uint32_t kTcPOff = kTcQOff + 2 * 4096;
 constexpr uint32_t kTcPBuf = 8192;        // one P^T tile of up to 32 rows
 constexpr uint32_t kTcBarOff = kTcPOff + 2 * kTcPBuf;
-constexpr uint32_t kTcMiscOff = kTcBarOff + 256;
+constexpr uint32_t kTcMiscOff = kTcBarOff + 512;  // 34 barriers, the unit ring, the schedule
 constexpr uint32_t kTcPrefixOff = kTcMiscOff + 5120;
 constexpr uint32_t kTcTmemCols = 128;
 
@@ -489,9 +500,10 @@ struct TcArgs {
     const int32_t *seq_lens;
     const void *query;
     void *out;
-    uint32_t *counters;     // [batch * kv_heads] tickets of the in-kernel merge
-    float *part_ml;         // [kTcMaxGrid][2 slots][16 heads][m, l]
-    float *part_o;          // [kTcMaxGrid][2 slots][16 heads][128]
+    uint32_t *counters;     // [kTcMaxUnits] tickets of the in-kernel merge, by first unit
+    uint32_t *claim;        // [2]: next dynamic unit, CTAs done claiming (zero between launches)
+    float *part_ml;         // [units][2 slots][GV heads][m, l]
+    float *part_o;          // [units][2 slots][GV heads][128]
     int32_t *tile_prefix;   // [batch + 1] copy of the tile prefix for the merge kernel
     int32_t table_stride;
     int32_t batch;
@@ -505,6 +517,9 @@ struct TcArgs {
     // Query heads h < pair_split of a segment use its dims 0-63, the others
     // dims 64-127; outputs are rows of 64.  0: head_dim 128, rows of 128.
     int32_t pair_split;
+    // dynamic tail: smallest unit (tiles; bounds the pieces of one segment),
+    // 0 = static units only
+    int32_t min_unit;
 };
 
 // Tensor maps of one launch: K and V pools (one page x 64 columns per box)
@@ -514,29 +529,86 @@ struct TcMaps {
 };
 
 struct TcWorkspace {
-    size_t counters, ml, o, prefix, total;
+    size_t claim, counters, prefix, ml, o, total;
 };
 
-TcWorkspace tc_workspace(size_t batch, size_t kv_heads) {
+// Scratch of one launch.  The claim words and the merge tickets (zero between
+// launches) sit at fixed offsets whatever the batch, so a workspace may serve
+// calls of any batch and head count it is large enough for; the partials of
+// `units` work units of `heads` query heads follow and need no zeroing.
+TcWorkspace tc_workspace(size_t units, size_t heads) {
     TcWorkspace w;
-    w.counters = 0;
-    w.ml = round_up(batch * kv_heads * sizeof(uint32_t), 256);
-    w.o = w.ml + round_up((size_t)kTcMaxGrid * 2 * 16 * 2 * sizeof(float), 256);
-    w.prefix = w.o + round_up((size_t)kTcMaxGrid * 2 * 16 * 128 * sizeof(float), 256);
-    w.total = w.prefix + round_up((batch + 1) * sizeof(int32_t), 256);
+    w.claim = 0;
+    w.counters = 256;
+    w.prefix = w.counters + round_up((size_t)kTcMaxUnits * sizeof(uint32_t), 256);
+    w.ml = w.prefix + round_up(((size_t)kTcMaxBatch + 1) * sizeof(int32_t), 256);
+    w.o = w.ml + round_up(units * 2 * heads * 2 * sizeof(float), 256);
+    w.total = w.o + round_up(units * 2 * heads * 128 * sizeof(float), 256);
     return w;
 }
 
-__device__ __forceinline__ int64_t range_start(int cta, int ncta, int64_t T) {
-    return T * cta / ncta;
+// Work units of one launch; every CTA (and the merge kernel) derives the same
+// schedule from T, the grid and the smallest unit.
+struct Sched {
+    int64_t T, S;  // tiles; static region [0, S)
+    int n;         // working CTAs = static units
+    int rounds;    // dynamic rounds of n units each
+    int size[kMaxRounds];
+};
+
+// Written in place (shared memory in the decode kernel: no local copy).
+__host__ __device__ inline void make_sched(Sched &s, int64_t T, int grid, int min_unit) {
+    s.T = T;
+    s.n = (int)(T < (int64_t)grid ? (T > 1 ? T : 1) : grid);
+    s.rounds = 0;
+    int64_t dyn = 0;
+    // an eighth of a CTA's share first, halving down to min_unit: the
+    // dynamic tiles stay under a quarter of T, every unit >= min_unit
+    int64_t sz = T / ((int64_t)s.n * 8);
+    if (min_unit > 0 && sz >= min_unit) {
+        while (s.rounds < kMaxRounds) {
+            const int64_t cur = sz > min_unit ? sz : min_unit;
+            s.size[s.rounds++] = (int)cur;
+            dyn += cur * s.n;
+            if (cur == min_unit) break;
+            sz >>= 1;
+        }
+    }
+    s.S = T - dyn;
 }
-// The CTA whose range holds tile t.
-__device__ __forceinline__ int cta_of_tile(int64_t t, int ncta, int64_t T) {
-    return (int)(((t + 1) * ncta - 1) / T);
+
+__host__ __device__ inline int sched_units(const Sched &s) { return s.n * (1 + s.rounds); }
+
+// First tile of unit u (T for u == sched_units).
+__device__ __forceinline__ int64_t unit_start(const Sched &s, int u) {
+    if (u < s.n) return s.S * u / s.n;
+    int64_t off = s.S;
+    int k = u - s.n;
+    for (int r = 0; r < s.rounds; ++r) {
+        if (k < s.n) return off + (int64_t)k * s.size[r];
+        off += (int64_t)s.n * s.size[r];
+        k -= s.n;
+    }
+    return s.T;
 }
-// Partial slot a CTA used for the piece of the segment starting at tile `seg`.
-__device__ __forceinline__ int piece_slot(int cta, int64_t seg, int ncta, int64_t T) {
-    return range_start(cta, ncta, T) < seg ? 1 : 0;
+
+// The unit that holds tile t.
+__device__ __forceinline__ int unit_of_tile(const Sched &s, int64_t t) {
+    if (t < s.S) return (int)(((t + 1) * s.n - 1) / s.S);
+    int64_t off = t - s.S;
+    int u = s.n;
+    for (int r = 0; r < s.rounds; ++r) {
+        const int64_t span = (int64_t)s.n * s.size[r];
+        if (off < span) return u + (int)(off / s.size[r]);
+        off -= span;
+        u += s.n;
+    }
+    return u;
+}
+
+// Partial slot a unit used for the piece of the segment starting at tile `seg`.
+__device__ __forceinline__ int unit_slot(const Sched &s, int u, int64_t seg) {
+    return unit_start(s, u) < seg ? 1 : 0;
 }
 
 // Exclusive prefix of tiles per sequence times kv_heads (0 for empty ones).
@@ -601,7 +673,8 @@ template <>
 struct IsBf16<__nv_bfloat16> { static constexpr bool value = true; };
 
 // Merges the partials of heads [h0, h0 + nh) of segment (b, g) into `out`
-// (nh rows of 128).  Every piece's (m, l) per head is staged in shared memory
+// (nh rows of 128); `heads` is the head stride of a partial slot (the GV of
+// the decode kernel).  Every piece's (m, l) per head is staged in shared memory
 // (`wst`, `lst`: np * nh floats each); one warp per head, lanes over the
 // pieces, turns them into weights exp2(m_c - m) / l; then each output float4
 // is the weighted sum of the pieces' partial rows: `ps` threads share one
@@ -609,22 +682,22 @@ struct IsBf16<__nv_bfloat16> { static constexpr bool value = true; };
 // ps * nh * 32 float4s), each keeping up to 16 loads in flight.  `tid`/`nthr`
 // are the participating threads (whole warps); `sync` is their barrier.
 template <typename OT, typename Sync>
-__device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, int64_t seg, int nt,
-                                              int ncta, int64_t T, int tid, int nthr, int ps,
-                                              float *wst, float *lst, int *slot, float4 *red,
-                                              int cap, OT *out, Sync sync) {
-    const int first = cta_of_tile(seg, ncta, T);
-    const int np = cta_of_tile(seg + nt - 1, ncta, T) - first + 1;
-    if (np > cap) {  // cannot happen with the host's choice of merge mode
+__device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, int heads,
+                                              int64_t seg, int nt, const Sched &sc, int tid,
+                                              int nthr, int ps, float *wst, float *lst, int *slot,
+                                              float4 *red, int cap, OT *out, Sync sync) {
+    const int first = unit_of_tile(sc, seg);
+    const int np = unit_of_tile(sc, seg + nt - 1) - first + 1;
+    if (np > cap) {  // cannot happen with the host's choice of merge mode and unit sizes
         if (tid == 0) record_fault(&g_decode_fault, kFaultPositionOutOfRange);
         return;
     }
-    for (int c = tid; c < np; c += nthr) slot[c] = piece_slot(first + c, seg, ncta, T);
+    for (int c = tid; c < np; c += nthr) slot[c] = unit_slot(sc, first + c, seg);
     sync();
     for (int i = tid; i < np * nh; i += nthr) {
         const int c = i / nh, h = h0 + (i - c * nh);
         const float2 ml = __ldcg(reinterpret_cast<const float2 *>(
-            a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * 16 + h) * 2));
+            a.part_ml + (((int64_t)(first + c) * 2 + slot[c]) * heads + h) * 2));
         wst[i] = ml.x;
         lst[i] = ml.y;
     }
@@ -660,7 +733,7 @@ __device__ __forceinline__ void merge_segment(const TcArgs &a, int h0, int nh, i
                 for (int i = 0; i < 16; ++i) {
                     const int c = c0 + i * ps;
                     v[i] = c < np ? __ldcg(reinterpret_cast<const float4 *>(
-                                        a.part_o + (((int64_t)(first + c) * 2 + slot[c]) * 16 +
+                                        a.part_o + (((int64_t)(first + c) * 2 + slot[c]) * heads +
                                                     h0 + hh) * 128 + d))
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
@@ -731,9 +804,15 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     uint64_t *p_full = bars + 10, *o_full = bars + 12, *o_empty = bars + 14;
     uint64_t *q_full = bars + 16, *q_empty = bars + 18;
     uint64_t *vfull = bars + 20, *vempty = bars + 23;
+    // unit ids from the K producer (which claims them) to the V producer, the
+    // MMA thread and the softmax group, in claim order
+    uint64_t *ring_full = bars + 26, *ring_empty = bars + 30;
+    volatile int *ring = reinterpret_cast<volatile int *>(sm + kTcBarOff + 288);  // kRing ints
+    Sched *sched = reinterpret_cast<Sched *>(sm + kTcBarOff + 320);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kTcMiscOff);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kTcMiscOff + 4);
     int *ticket = reinterpret_cast<int *>(sm + kTcMiscOff + 8);
+    volatile int *group_unit = reinterpret_cast<volatile int *>(sm + kTcMiscOff + 12);
     int *scan = reinterpret_cast<int *>(sm + kTcMiscOff + 32);    // 8 ints
     float *red = reinterpret_cast<float *>(sm + kTcMiscOff + 64);  // [2][4][16]
     float *lred = red + 128;                                        // [4][16]
@@ -759,6 +838,10 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             mbar_init(&q_full[i], 1);
             mbar_init(&q_empty[i], 1);
         }
+        for (int i = 0; i < kRing; ++i) {
+            mbar_init(&ring_full[i], 1);
+            mbar_init(&ring_empty[i], 3);  // V producer, MMA thread, softmax group
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -779,6 +862,13 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     // here on global memory written by earlier kernels (pages, tables,
     // lengths, queries) is read.
     pdl_wait();
+    // Dependents (the next step's staging and append, the merge kernel) may
+    // launch now: they start only once every CTA of this grid has run this
+    // line, i.e. once all of them are resident, so none can hold an SM a CTA
+    // of this grid still needs; each runs griddepcontrol.wait before it
+    // touches anything this grid reads or writes, and meanwhile takes the
+    // shared memory the CTAs of this grid leave over or free as they finish.
+    pdl_launch_dependents();
     build_tile_prefix(a, prefix, scan);
     fence_proxy_async_smem();
     tc_fence_before();
@@ -786,12 +876,13 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int64_t total_tiles = prefix[a.batch];
+    if (tid == 0) make_sched(*sched, total_tiles, (int)gridDim.x, a.min_unit);
+    __syncthreads();
+    const Sched &sc = *sched;
     // CTAs past the tile count idle, so every working CTA owns >= 1 tile and
-    // the CTAs spanned by a segment are exactly its pieces.
-    const int ncta = (int)min((int64_t)gridDim.x, max(total_tiles, (int64_t)1));
-    const bool works = (int)blockIdx.x < ncta && total_tiles > 0;
-    const int64_t my_start = works ? range_start(blockIdx.x, ncta, total_tiles) : 0;
-    const int64_t my_end = works ? range_start(blockIdx.x + 1, ncta, total_tiles) : 0;
+    // the units spanned by a segment are exactly its pieces.
+    const bool works = (int)blockIdx.x < sc.n && total_tiles > 0;
+    const int n_units = sched_units(sc);
     const int q_heads = a.kv_heads * GV;
     uint32_t *fault = &g_decode_fault;
     if (blockIdx.x == 0 && a.tile_prefix != nullptr)
@@ -831,11 +922,27 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         // Also stages each piece's query rows (the B operand of QK^T).
         uint32_t j = 0, qi = 0;
         bool ok = true;
-        for (int64_t t = my_start; ok && t < my_end;) {
-            const Piece P = piece_at(t, my_end, prefix, a);
+        int u = works ? (int)blockIdx.x : -1;
+        for (uint32_t ku = 0;; ++ku) {
+            // publish the unit (-1: no more) to the other roles
+            const int rs = (int)(ku % kRing);
+            if (!mbar_wait(&ring_empty[rs], ((ku / kRing) & 1) ^ 1, abort_flag, fault)) ok = false;
+            if (!ok) u = -1;
+            if (lane == 0) {
+                ring[rs] = u;
+                mbar_arrive(&ring_full[rs]);
+            }
+            __syncwarp();
+            if (u < 0) break;
+            const int64_t ue = unit_start(sc, u + 1);
+        for (int64_t t = unit_start(sc, u); ok && t < ue;) {
+            const Piece P = piece_at(t, ue, prefix, a);
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
-            if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) break;
+            if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) {
+                ok = false;
+                break;
+            }
             if (lane == 0) {  // G query rows, two 64-column halves, 128-byte swizzle
                 unsigned char *qb = sm + kTcQOff + (qi & 1) * 4096;
                 const int32_t qrow = a.q_row0 + P.b * q_heads + P.g * GV;
@@ -863,14 +970,42 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             }
             ++qi;
         }
+            // claim the next dynamic unit (this CTA's loads of the current one
+            // are issued, its last tiles still stream)
+            int next = -1;
+            if (ok && sc.rounds > 0 && lane == 0) {
+                const int c = sc.n + (int)atomicAdd(a.claim, 1u);
+                next = c < n_units ? c : -1;
+            }
+            u = __shfl_sync(0xffffffffu, next, 0);
+        }
+        // The last CTA done claiming zeroes the claim words for the next launch
+        // (every CTA's final claim precedes its count here).
+        if (sc.rounds > 0 && works && lane == 0) {
+            __threadfence();
+            if (atomicAdd(a.claim + 1, 1u) == (uint32_t)sc.n - 1) {
+                atomicExch(a.claim, 0u);
+                atomicExch(a.claim + 1, 0u);
+            }
+        }
     } else if (warp == 6) {
         // ---------------------------- V producer ----------------------------
         // V slots free later than K slots (after the PV, not the QK^T), so the
         // two rings run on their own barriers and K loads can run ahead.
         uint32_t j = 0;
         bool ok = true;
-        for (int64_t t = my_start; ok && t < my_end;) {
-            const Piece P = piece_at(t, my_end, prefix, a);
+        for (uint32_t ku = 0; ok; ++ku) {
+            const int rs = (int)(ku % kRing);
+            int u = -1;
+            if (lane == 0) {
+                if (mbar_wait(&ring_full[rs], (ku / kRing) & 1, abort_flag, fault)) u = ring[rs];
+                mbar_arrive(&ring_empty[rs]);
+            }
+            u = __shfl_sync(0xffffffffu, u, 0);
+            if (u < 0) break;
+            const int64_t ue = unit_start(sc, u + 1);
+        for (int64_t t = unit_start(sc, u); ok && t < ue;) {
+            const Piece P = piece_at(t, ue, prefix, a);
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
@@ -884,15 +1019,26 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                           L, P.g);
             }
         }
+        }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
             uint32_t j = 0, qi = 0;
             bool ok = true;
-            for (int64_t t = my_start; ok && t < my_end;) {
-                const Piece P = piece_at(t, my_end, prefix, a);
+            for (uint32_t ku = 0; ok; ++ku) {
+                const int rs = (int)(ku % kRing);
+                int u = -1;
+                if (mbar_wait(&ring_full[rs], (ku / kRing) & 1, abort_flag, fault)) u = ring[rs];
+                mbar_arrive(&ring_empty[rs]);
+                if (u < 0) break;
+                const int64_t ue = unit_start(sc, u + 1);
+            for (int64_t t = unit_start(sc, u); ok && t < ue;) {
+                const Piece P = piece_at(t, ue, prefix, a);
                 t += P.k1 - P.k0;
-                if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag, fault)) break;
+                if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag, fault)) {
+                    ok = false;
+                    break;
+                }
                 const uint32_t qaddr = smem_u32(sm + kTcQOff + (qi & 1) * 4096);
                 // PV of tile jp: O^T[buf] = V^T . P^T once the group wrote P
                 // and read the O of tile jp - 2 out of that buffer.
@@ -945,6 +1091,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 if (ok && P.k1 > P.k0 && !issue_pv(j - 1)) ok = false;
                 ++qi;
             }
+            }
         }
         __syncwarp();
     } else if (warp < 6) {
@@ -959,9 +1106,22 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         auto group_sync = [] { named_barrier(1, 128); };
         uint32_t j = 0;
         bool aborted = false;
-        for (int64_t t = my_start; t < my_end;) {
-            const Piece P = piece_at(t, my_end, prefix, a);
-            const bool first_piece = t == my_start;
+        for (uint32_t ku = 0;; ++ku) {
+            const int rs = (int)(ku % kRing);
+            if (wt == 0) {
+                int uu = -1;
+                if (mbar_wait(&ring_full[rs], (ku / kRing) & 1, abort_flag, fault)) uu = ring[rs];
+                *group_unit = uu;
+                mbar_arrive(&ring_empty[rs]);
+            }
+            group_sync();
+            const int u = *group_unit;
+            group_sync();  // read by all before thread 0 of the group writes the next one
+            if (u < 0) break;
+            const int64_t us = unit_start(sc, u), ue = unit_start(sc, u + 1);
+        for (int64_t t = us; t < ue;) {
+            const Piece P = piece_at(t, ue, prefix, a);
+            const bool first_piece = t == us;
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
             float m_run[GV], l_part[GV], acc[GV];
@@ -1078,7 +1238,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 continue;
             }
             const int kslot = first_piece ? 0 : 1;
-            const int64_t slot = ((int64_t)blockIdx.x * 2 + kslot) * 16;
+            const int64_t slot = ((int64_t)u * 2 + kslot) * GV;
 #pragma unroll
             for (int h = 0; h < GV; ++h) {
                 a.part_o[(slot + h) * 128 + row] = acc[h];
@@ -1088,21 +1248,24 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 }
             }
             if (!a.merge_in_kernel) continue;
-            const int np = cta_of_tile(P.seg + P.nt - 1, ncta, total_tiles) -
-                           cta_of_tile(P.seg, ncta, total_tiles) + 1;
+            // a unit is the first unit of at most one cut segment (the last
+            // segment starting in it), so the first unit names the ticket
+            const int u0 = unit_of_tile(sc, P.seg);
+            const int np = unit_of_tile(sc, P.seg + P.nt - 1) - u0 + 1;
             group_sync();
             if (wt == 0) {
                 __threadfence();  // publishes the group's partials (bar.sync is cumulative)
-                const uint32_t tk = atomicAdd(a.counters + (int64_t)P.b * a.kv_heads + P.g, 1u);
+                const uint32_t tk = atomicAdd(a.counters + u0, 1u);
                 *ticket = tk == (uint32_t)(np - 1);
             }
             group_sync();
             if (*ticket) {
                 __threadfence();
-                merge_segment<OT>(a, 0, GV, P.seg, P.nt, ncta, total_tiles, wt, 128, 1, mwst,
-                                  mlst, mslot, nullptr, kInKernelMergeMax, out, group_sync);
-                if (wt == 0) a.counters[(int64_t)P.b * a.kv_heads + P.g] = 0u;
+                merge_segment<OT>(a, 0, GV, GV, P.seg, P.nt, sc, wt, 128, 1, mwst, mlst, mslot,
+                                  nullptr, kInKernelMergeMax, out, group_sync);
+                if (wt == 0) a.counters[u0] = 0u;
             }
+        }
         }
         // empty sequences: no tile, zero output (the SDK's all-masked rule)
         for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
@@ -1127,6 +1290,7 @@ template <typename OT>
 __global__ void __launch_bounds__(kMergeThreads)
 pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     pdl_wait();
+    pdl_launch_dependents();  // e.g. the all-gather of the merged heads
     __shared__ float wst[kTcMaxGrid];
     __shared__ float lst[kTcMaxGrid];
     __shared__ int slot[kTcMaxGrid];
@@ -1134,15 +1298,17 @@ pkv_tc_merge_kernel(const TcArgs a, int group, int grid) {
     const int b = blockIdx.y;
     const int g = blockIdx.x / group, h = blockIdx.x - g * group;
     const int64_t T = a.tile_prefix[a.batch];
-    const int ncta = (int)min((int64_t)grid, max(T, (int64_t)1));  // as the decode kernel
+    __shared__ Sched sc;
+    if (threadIdx.x == 0) make_sched(sc, T, grid, a.min_unit);  // as the decode kernel
+    __syncthreads();
     const int nt = (a.tile_prefix[b + 1] - a.tile_prefix[b]) / a.kv_heads;
     if (nt == 0 || T == 0) return;
     const int64_t seg = a.tile_prefix[b] + (int64_t)g * nt;
-    if (cta_of_tile(seg, ncta, T) == cta_of_tile(seg + nt - 1, ncta, T)) return;
+    if (unit_of_tile(sc, seg) == unit_of_tile(sc, seg + nt - 1)) return;
     OT *out = static_cast<OT *>(a.out) +
               ((int64_t)b * a.kv_heads * group + (int64_t)g * group + h) *
                   (a.pair_split != 0 ? 64 : 128);
-    merge_segment<OT>(a, h, 1, seg, nt, ncta, T, threadIdx.x, kMergeThreads, kMergeThreads / 32,
+    merge_segment<OT>(a, h, 1, group, seg, nt, sc, threadIdx.x, kMergeThreads, kMergeThreads / 32,
                       wst, lst, slot, red, kTcMaxGrid, out, [] { __syncthreads(); });
 }
 
@@ -1159,16 +1325,23 @@ int sm_count() {
     return g_sm_count[dev];
 }
 
+// Grid of the tensor-core decode kernel and its work units.
+int tc_grid() { return sm_count() < kTcMaxGrid ? sm_count() : kTcMaxGrid; }
+size_t tc_units(int grid, bool dynamic) { return (size_t)grid * (dynamic ? 1 + kMaxRounds : 1); }
+
 
 struct WsLayout {
     size_t counters, ml, o, total;
 };
 
-WsLayout ws_layout(size_t batch, size_t q_heads, size_t kv_heads, size_t head_dim,
-                   size_t max_chunks) {
+// The tickets ([batch][kv_heads], zero between launches) get room for
+// kMaxBatch sequences of q_heads heads whatever this call's batch, so the
+// partials of an earlier, smaller call never sit where a later call's
+// tickets are.
+WsLayout ws_layout(size_t batch, size_t q_heads, size_t head_dim, size_t max_chunks) {
     WsLayout w;
     w.counters = 0;
-    w.ml = round_up(batch * kv_heads * sizeof(uint32_t), 256);
+    w.ml = round_up((size_t)kMaxBatch * q_heads * sizeof(uint32_t), 256);
     w.o = w.ml + round_up(batch * q_heads * max_chunks * 2 * sizeof(float), 256);
     w.total = w.o + round_up(batch * q_heads * max_chunks * head_dim * sizeof(float), 256);
     return w;
@@ -1253,9 +1426,10 @@ int launch_tc(const TcArgs &args, const TcMaps &mp, int ncta,
         configured[dev] = 1;
     }
     // Programmatic dependent launch: the prologue (barriers, TMEM, shared
-    // memory) overlaps the tail of the kernel before it in the stream.  The
-    // decode kernel itself never releases its dependents early: a merge CTA
-    // waiting on an SM could keep a decode CTA from being placed.
+    // memory) overlaps the tail of the kernel before it in the stream, and
+    // the kernel releases its own dependents once all its CTAs are resident
+    // (the merge kernel and the next step's staging then launch while it
+    // streams and wait on griddepcontrol.wait).
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1345,10 +1519,10 @@ size_t pkv_decode_workspace_bytes(size_t batch, size_t q_heads, size_t head_dim,
                                   size_t max_seq_len, size_t chunk_tokens) {
     const size_t chunk = pkv::pick_chunk(chunk_tokens, max_seq_len);
     const size_t max_chunks = max_seq_len / chunk + 1;
-    // kv_heads only sizes the ticket counters; q_heads bounds it.  The larger
-    // of the two kernels' layouts, so either may run.
-    const size_t simt = pkv::ws_layout(batch, q_heads, q_heads, head_dim, max_chunks).total;
-    const size_t tc = pkv::tc_workspace(batch, q_heads).total;
+    // The larger of the two kernels' layouts, so either may run; the tensor-
+    // core one with room for the dynamic tail's units and 16 heads a segment.
+    const size_t simt = pkv::ws_layout(batch, q_heads, head_dim, max_chunks).total;
+    const size_t tc = pkv::tc_workspace(pkv::tc_units(pkv::tc_grid(), true), 16).total;
     return simt > tc ? simt : tc;
 }
 
@@ -1422,9 +1596,16 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
     }
     const size_t chunk = pkv::pick_chunk(chunk_tokens, max_seq_len);
     const size_t max_chunks = max_seq_len / chunk + 1;
-    const pkv::WsLayout ws = pkv::ws_layout(batch->batch, q_heads, kvh, hd, max_chunks);
-    const pkv::TcWorkspace tws = pkv::tc_workspace(batch->batch, kvh);
-    const size_t need = use_tc ? tws.total : ws.total;
+    const pkv::WsLayout ws = pkv::ws_layout(batch->batch, q_heads, hd, max_chunks);
+    // tensor-core path: the static units' layout is the minimum; the dynamic
+    // tail also needs the partials of its rounds' units
+    const int ncta = pkv::tc_grid();
+    const size_t gv = hd == 64 ? 2 * group : group;  // query heads of one segment
+    const pkv::TcWorkspace tws_static = pkv::tc_workspace(pkv::tc_units(ncta, false), gv);
+    const pkv::TcWorkspace tws_dyn = pkv::tc_workspace(pkv::tc_units(ncta, true), gv);
+    const bool dyn_fits = workspace_bytes >= tws_dyn.total;
+    const pkv::TcWorkspace tws = dyn_fits ? tws_dyn : tws_static;
+    const size_t need = use_tc ? tws_static.total : ws.total;
     if (workspace == nullptr || workspace_bytes < need || ((uintptr_t)workspace % 256) != 0) {
         pkv_internal_set_error(error, error_capacity,
                                "%s: workspace needs %zu bytes, 256-byte aligned (got %zu)", what,
@@ -1472,9 +1653,9 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
             pkv_internal_set_error(error, error_capacity, "%s: tensor map encoding failed", what);
             return 0;
         }
-        const int ncta = pkv::sm_count() < pkv::kTcMaxGrid ? pkv::sm_count() : pkv::kTcMaxGrid;
         auto *wsb = static_cast<unsigned char *>(workspace);
         pkv::TcArgs t;
+        t.claim = reinterpret_cast<uint32_t *>(wsb + tws.claim);
         t.counters = reinterpret_cast<uint32_t *>(wsb + tws.counters);
         t.part_ml = reinterpret_cast<float *>(wsb + tws.ml);
         t.part_o = reinterpret_cast<float *>(wsb + tws.o);
@@ -1496,6 +1677,19 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         const bool fits = ncta / (int)segs + 2 <= pkv::kInKernelMergeMax;
         const bool many_segments = batch->batch * segs * 2 >= (size_t)ncta;
         t.merge_in_kernel = fits && many_segments;
+        // Dynamic tail (in-kernel merges only): every unit holds at least
+        // min_unit tiles, so a segment of at most max_tiles tiles meets at
+        // most max_tiles / min_unit + 2 <= kInKernelMergeMax units.  Each
+        // piece costs the CTA a pipeline drain at its end (the last PV, the
+        // l reduction, partial stores, a ticket), so units are never below
+        // kMinUnitTiles and short launches (a CTA share under ~64 tiles,
+        // below 8 * kMinUnitTiles) keep the static split.
+        const size_t max_tiles = (max_seq_len + pkv::kTcTile - 1) / pkv::kTcTile;
+        const size_t by_pieces = (max_tiles + 23) / 24;
+        t.min_unit = t.merge_in_kernel && dyn_fits
+                         ? (int32_t)(by_pieces > pkv::kMinUnitTiles ? by_pieces
+                                                                    : pkv::kMinUnitTiles)
+                         : 0;
         // launches of at most kTcMaxBatch sequences (their prefix lives in smem)
         const size_t osz = output_dtype == PKV_DTYPE_F32 ? 4 : 2;
         ok = 1;
@@ -1510,7 +1704,6 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
             sl.query = static_cast<const char *>(query) + b0 * q_heads * hd * 2;
             sl.q_row0 = (int32_t)(b0 * q_heads);
             sl.out = static_cast<char *>(output) + b0 * q_heads * hd * osz;
-            sl.counters = t.counters + b0 * segs;
             ok = pkv::dispatch_tc(sl, (int)group, pair, bf16, output_dtype, mp, ncta, s);
         }
     } else if (layer->dtype == PKV_DTYPE_F16)
@@ -1651,13 +1844,19 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
     // Scratch of the kernel pkv_paged_decode will pick for this shape;
     // anything above the array is refused.
     const size_t group = q_heads / kvh;
-    size_t need;
+    size_t need, tickets;
     if (pkv::tc_eligible(hd, kvh, layer->block_size, group,
                          layer->block_count * layer->block_size)) {
-        need = pkv::tc_workspace(batch->batch, kvh).total;
+        // the static units' layout; the dynamic tail runs when its larger
+        // layout fits the array as well
+        const pkv::TcWorkspace w =
+            pkv::tc_workspace(pkv::tc_units(pkv::tc_grid(), false), hd == 64 ? 2 * group : group);
+        need = w.total;
+        tickets = w.prefix;  // claim words and tickets
     } else {
         const size_t chunk = pkv::pick_chunk(0, max_seq_len);
-        need = pkv::ws_layout(batch->batch, q_heads, kvh, hd, max_seq_len / chunk + 1).total;
+        need = pkv::ws_layout(batch->batch, q_heads, hd, max_seq_len / chunk + 1).total;
+        tickets = pkv::round_up(batch->batch * kvh * sizeof(uint32_t), 256);
     }
     if (need > kDecodeStaticScratchBytes) {
         pkv_internal_set_error(error, error_capacity,
@@ -1668,12 +1867,11 @@ extern "C" int pkv_paged_decode_static_scratch(const PkvPagedLayer *layer, const
     }
     void *scratch = static_scratch_for_current_device(error, error_capacity);
     if (scratch == nullptr) return 0;
-    // The split-K tickets must be zero when a decode starts; both layouts
-    // keep them first.  A decode that completes leaves them at zero, but one
-    // that gave up part-way (a bounded wait that expired) may not, and the
-    // array outlives every call, so each call clears them (one small memset
-    // on the caller's stream).
-    const size_t tickets = pkv::round_up(batch->batch * kvh * sizeof(uint32_t), 256);
+    // The split-K tickets (and the dynamic tail's claim words) must be zero
+    // when a decode starts; both layouts keep them first.  A decode that
+    // completes leaves them at zero, but one that gave up part-way (a bounded
+    // wait that expired) may not, and the array outlives every call, so each
+    // call clears them (one small memset on the caller's stream).
     const cudaError_t st = cudaMemsetAsync(scratch, 0, tickets, (cudaStream_t)stream);
     if (st != cudaSuccess) {
         pkv_internal_set_error(error, error_capacity, "%s: clearing the tickets failed: %s", what,

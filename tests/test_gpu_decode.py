@@ -213,8 +213,27 @@ def test_workspace_stays_reusable(lib, oracle_mod, cuda):
         P.paged_decode(case.layer(), case.batch(), case.d_q, out, case.scale, 1000, ws, 64)
         torch.cuda.synchronize()
         check_close(out.cpu().numpy(), want, "repeat")
-    counters = ws[: 3 * 2 * 4].cpu().numpy()
+    counters = ws[: 256 + 6144].cpu().numpy()  # claim words and tickets
     assert not counters.any()
+
+
+def test_workspace_serves_growing_batches(lib, oracle_mod, cuda):
+    """One scratch, made once for the largest batch, serves calls whose batch
+    grows and shrinks: the tickets and the dynamic tail's claim words sit at
+    fixed offsets, never where an earlier call left partials.  Every call has
+    enough segments for in-kernel merges; the long ones (16 sequences of up to
+    30k tokens, ~100 tiles a CTA) also run the dynamic tail."""
+    import torch
+    ws = P.decode_workspace(16, 32, 128, 30000, device=cuda)
+    for b, top, seed in [(10, 3000, 61), (16, 30000, 62), (10, 3000, 63), (16, 30000, 64)]:
+        rng = np.random.default_rng(seed)
+        case = PagedCase(rng.integers(1, top, b), 32, 8, 128, 16, "f16", seed=seed, device=cuda)
+        out = torch.full((b, 32, 128), float("nan"), dtype=torch.float32, device=cuda)
+        P.paged_decode(case.layer(), case.batch(), case.d_q, out, case.scale, 30000, ws)
+        torch.cuda.synchronize()
+        check_close(out.cpu().numpy(), _oracle(case, oracle_mod), f"batch {b}")
+        assert not ws[: 256 + 6144].cpu().numpy().any()
+    assert P.device_fault(0) == 0
 
 
 def test_cfg2_full_size(lib, oracle_mod, cuda):

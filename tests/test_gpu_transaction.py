@@ -231,3 +231,73 @@ def test_large_staging_spreads_over_ctas(lib, cuda):
     assert np.array_equal(to_host_bits(v), to_host_bits(torch.cat(rows_v)))
     assert P.device_fault(0) == 0
     cache.free()
+
+
+def test_decode_stepper_back_to_back(lib, oracle_mod, cuda):
+    """DecodeStepper steps queued back to back with no host synchronisation:
+    the decode kernel releases its dependents early, so each step's staging
+    and append launch while the previous decode still streams.  Every step's
+    output (its own buffer) must match the oracle on the pages as they were
+    at that step, and the pages must end bit-exact.  A step whose decode
+    call is refused rolls back."""
+    import torch
+    n, kvh, qh, d, steps = 8, 2, 8, 128, 24
+    cache = P.PagedKVCache(16, 1024, n)
+    pool = P.PagedPool(cache, 0, P.PKV_DTYPE_F16, 1, kvh, d, n, 160)
+    layer = pool.layer(0)
+    seqs = [cache.sequence_create() for _ in range(n)]
+    past = [300 + 217 * b for b in range(n)]
+    for r in range(1, 160):  # interleaved reservations: fragmented tables
+        for s, L in zip(seqs, past):
+            if 16 * (r - 1) < L:
+                cache.reserve(s, min(L, 16 * r))
+    kv = kvh * d
+    host_k = W.normal_bits(71, (sum(past), kv), "f16", stream=1)
+    host_v = W.normal_bits(71, (sum(past), kv), "f16", stream=2)
+    pool.step_begin(seqs, past)
+    P.kv_import(layer, pool.step_batch(), to_device_bits(host_k, "f16", cuda),
+                to_device_bits(host_v, "f16", cuda), pool.step_row_offsets())
+    pool.step_end(True)
+    mk = np.zeros((1024 * 16, kv), np.uint16)
+    mv = np.zeros_like(mk)
+    offs = np.concatenate([[0], np.cumsum(past)]).astype(np.int32)
+    oracle_mod.kv_rows(mk, mv, 16, _tables(cache, seqs, 160), np.array(past), offs, host_k.copy(),
+                       host_v.copy(), to_pool=True, tail=False)
+    nks = [W.normal_bits(500 + i, (n, kv), "f16", stream=3) for i in range(steps)]
+    nvs = [W.normal_bits(500 + i, (n, kv), "f16", stream=4) for i in range(steps)]
+    qs = [W.normal_bits(500 + i, (n, qh, d), "f16", stream=5) for i in range(steps)]
+    dk = [to_device_bits(x, "f16", cuda) for x in nks]
+    dv = [to_device_bits(x, "f16", cuda) for x in nvs]
+    dq = [to_device_bits(x, "f16", cuda) for x in qs]
+    outs = [torch.empty(n, qh, d, dtype=torch.float32, device=cuda) for _ in range(steps)]
+    max_len = max(past) + steps + 1
+    ws = P.decode_workspace(n, qh, d, max_len, device=cuda)
+    scale = float(1 / np.sqrt(d))
+    stepper = P.DecodeStepper(pool, layer, seqs, dq[0], dk[0], dv[0], outs[0], scale, max_len,
+                              ws)
+    for i in range(steps):
+        stepper.bind(dq[i], dk[i], dv[i], outs[i])
+        stepper.step()
+    torch.cuda.synchronize()
+    lengths = np.array(past)
+    for i in range(steps):
+        lengths = lengths + 1
+        tab = _tables(cache, seqs, 160)
+        oracle_mod.kv_rows(mk, mv, 16, tab, lengths, None, nks[i].copy(), nvs[i].copy(),
+                           to_pool=True, tail=True)
+        want = oracle_mod.paged_decode(qs[i], "f16", mk, mv, kvh, d, 16, tab, lengths, scale)
+        check_close(outs[i].cpu().numpy(), want, f"step {i}")
+    assert [cache.length(s) for s in seqs] == lengths.tolist()
+    k, v = dump_pool(layer, cuda)
+    assert np.array_equal(k, mk) and np.array_equal(v, mv)
+    # a refused decode (workspace too small) rolls the step back
+    small = torch.zeros(64, dtype=torch.uint8, device=cuda)
+    bad = P.DecodeStepper(pool, layer, seqs, dq[0], dk[0], dv[0], outs[0], scale, max_len, small)
+    with pytest.raises(P.PkvError, match="workspace"):
+        bad.step()
+    assert [cache.length(s) for s in seqs] == lengths.tolist()
+    assert all(cache.begin_decode(s) for s in seqs)
+    for s in seqs:
+        cache.end_decode(s)
+    assert P.device_fault(0) == 0
+    cache.free()
