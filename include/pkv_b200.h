@@ -120,9 +120,12 @@ int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes,
  * S = K.Q^T and O = V^T.P^T on tcgen05 with FP32 accumulators in TMEM, so
  * each page byte is read once for all q_heads/kv_heads query heads of its KV
  * head.  The 128-token tiles of all (sequence, KV head) segments form one
- * stream cut evenly across the CTAs (stream-K); a segment split between CTAs
- * is merged from FP32 partials (m, l, O) by the last CTA to finish it, or,
- * when few segments are cut into many pieces, by a separate merge kernel.
+ * stream (stream-K): most of it is cut evenly across the CTAs, and on long
+ * launches the last part is cut into smaller work units that CTAs claim as
+ * they finish, so SMs that stream faster take more.  A segment split between
+ * units is merged from FP32 partials (m, l, O) by the last CTA to finish a
+ * piece of it, or, when few segments are cut into many pieces, by a
+ * separate merge kernel.
  * head_dim 64 with an even KV-head count runs there too, KV heads 2g and
  * 2g+1 as one 128-column segment.  Other shapes (head_dim 64 with an odd
  * KV-head count, other page sizes) run a CUDA-core kernel: one CTA per

@@ -13,10 +13,11 @@
 //   its query heads.  P is written as a 16-bit high half plus the low
 //   remainder in the otherwise-zero rows of the N=16 operand (one MMA, ~22
 //   bits of P).  Work split is stream-K: the tiles of all (sequence, KV head)
-//   segments form one stream cut evenly across the CTAs; a segment cut
-//   between CTAs leaves FP32 partials (m, l, O) that the last CTA to finish
-//   it merges (atomic ticket), or, with few segments cut into many pieces,
-//   the separate pkv_tc_merge_kernel.
+//   segments form one stream, cut evenly across the CTAs up to a dynamic
+//   tail (long launches only) of smaller units that CTAs claim with an
+//   atomic as they finish; a segment cut between units leaves FP32 partials
+//   (m, l, O) that the last CTA to finish a piece merges (atomic ticket), or,
+//   with few segments cut into many pieces, the separate pkv_tc_merge_kernel.
 //
 // paged_decode_simt_kernel (head_dim 64 or 128, any page size): CUDA cores.
 //   Work unit = (sequence b, KV head g, chunk c of `chunk` positions); a
