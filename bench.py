@@ -7,8 +7,10 @@ of 16 tokens, context lengths LogNormal(ln 8192, sigma=0.5) clipped to
 balancing), every GPU with its own TensorPagedKVCache and device pool, no
 collective.  A step is the SDK's decode transaction for the whole shard:
 pkv_step_begin (decode locks, reserve one token per sequence, page-table
-patch upload), pkv_kv_append of the new K/V rows, pkv_paged_decode, and
-pkv_step_end (commit lengths, release locks).
+patch upload), pkv_paged_decode_append (the new K/V rows stored by the
+decode kernel itself, then paged SDPA; --unfused: pkv_kv_append and
+pkv_paged_decode as two calls), and pkv_step_end (commit lengths, release
+locks).
 
   value  tokens/s of the whole job with Q and new K/V rows already in HBM
          (total tokens of all ranks / max over ranks of the device step time)
@@ -71,6 +73,10 @@ def parse_args():
                         "deadline (pkv_comm_*), torch.distributed's all_gather_into_tensor "
                         "(NCCL), or the library's peer-store all-gather over NVLink "
                         "(pkv_peer_*, an A/B variant)")
+    p.add_argument("--unfused", action="store_true",
+                   help="decode configs: append with pkv_kv_append and decode with "
+                        "pkv_paged_decode (two launches) instead of the one-launch "
+                        "pkv_paged_decode_append (an A/B variant)")
     p.add_argument("--prefill-batch", type=int, default=0,
                    help="config 5 only: sequences per step (default: the config's 8; smaller "
                         "values make small cases for profiling)")
@@ -376,21 +382,22 @@ def run_ours(args) -> None:
     kv_bytes_per_token = c.kv_width * 2 * 2
 
     stepper = P.DecodeStepper(pool, layer, seqs, q, newk, newv, out, c.scale, max_len, ws, chunk,
-                              stream)
+                              stream, fused=not args.unfused)
 
     def step(i: int | None, bufs=None):
         """One SDK transaction for the shard: step_begin (one staging kernel),
-        append, paged decode, step_end, through the C ABI with the arguments
-        bound once (DecodeStepper).  Nothing else is put on the stream between
-        the kernels, so each one's launch and prologue overlap the one before
-        it (programmatic dependent launch)."""
+        append + paged decode (one kernel; two with --unfused), step_end,
+        through the C ABI with the arguments bound once (DecodeStepper).
+        Nothing else is put on the stream between the kernels, so each one's
+        launch and prologue overlap the one before it (programmatic dependent
+        launch)."""
         nonlocal cur
         if bufs is not None:
             stepper.bind(*bufs)
         stepper.step()
         cur = cur + 1
         if i is not None:
-            launches["n"] += 3  # staging, append, decode
+            launches["n"] += 3 if args.unfused else 2  # staging, (append,) decode
             bytes_log.append(float(cur.sum()) * kv_bytes_per_token + 2 * q.numel() * 2 +
                              float(((cur + 15) // 16).sum()) * 4)
 
@@ -493,8 +500,10 @@ def run_ours(args) -> None:
             e2e = {"value": total_seqs / (e2e_ms / 1e3), "unit": "tokens/s",
                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
                    "d2h_bytes_per_step": d2h * world,
-                   "api": "pkv_step_begin/pkv_kv_append/pkv_paged_decode/pkv_step_end "
-                          "(DecodeStepper) + pinned host<->device copies on a second stream, "
+                   "api": ("pkv_step_begin/pkv_kv_append/pkv_paged_decode/pkv_step_end"
+                           if args.unfused else
+                           "pkv_step_begin/pkv_paged_decode_append/pkv_step_end") +
+                          " (DecodeStepper) + pinned host<->device copies on a second stream, "
                           "double-buffered"}
     fault = P.device_fault(local)
     if fault:
@@ -822,7 +831,7 @@ def run_cfg4(args) -> None:
     cur = [L0]
 
     stepper = P.DecodeStepper(pool, layer, [seq], q, newk, newv, out, c.scale, max_len, ws, 0,
-                              stream)
+                              stream, fused=not args.unfused)
 
     def step(q_in=None, k_in=None, v_in=None, full_out=None):
         """Transaction, append, decode of this rank's heads (DecodeStepper:
@@ -988,8 +997,8 @@ def run_cfg4(args) -> None:
             "e2e": {"value": 1.0 / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": (h_q.numel() + h_k.numel() + h_v.numel()) * 2 * world,
                     "d2h_bytes_per_step": h_o.numel() * 2},
-            "gpu_launches": steps * (4 + (peer is not None)),  # staging, append, decode,
-                                                                 # merge (+ gather / NCCL's)
+            # staging, (append,) decode, merge (+ the peer gather; NCCL's own not counted)
+            "gpu_launches": steps * (3 + bool(args.unfused) + (peer is not None)),
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -149,7 +149,31 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch,
                      size_t workspace_bytes, PkvStream stream, char *error,
                      size_t error_capacity);
 
-/* Paged decode that allocates nothing: pkv_paged_decode with its scratch in
+/* A decode step's append and paged decode in one call: the same result as
+ * pkv_kv_append(layer, batch, NULL, key_rows, value_rows, batch->batch, ...)
+ * followed by pkv_paged_decode(...) on the same stream -- each sequence's new
+ * K/V row ([batch][kv_heads * head_dim], 16-byte aligned) is stored at
+ * position seq_lens[b] - 1, bit for bit as the append kernel stores it, and
+ * the decode attends over it.  On the tensor-core path this is one launch:
+ * the producer warp that loads the 128-token tile holding the new row first
+ * stores the row into its page (and fences it against the TMA that reads the
+ * page), so no separate append kernel sits between the step's staging and
+ * its decode.  Other shapes run the two kernels.  A sequence with
+ * seq_lens[b] == 0 has no room for its row: nothing is stored, its output is
+ * zeros and fault code 3 is recorded, as pkv_kv_append does.  Replaces the
+ * SDK backend's per-layer decode call: decode_rope_cache_kernel's K/V store
+ * (attention_cuda.cu:307-341; RoPE stays the caller's) and the three decode
+ * kernels (:343-398), launched at :996-1011. */
+int pkv_paged_decode_append(const PkvPagedLayer *layer, const PkvBatch *batch,
+                            const void *key_rows, const void *value_rows,
+                            size_t q_heads, const void *query, float scale,
+                            void *output, PkvDType output_dtype,
+                            size_t max_seq_len, size_t chunk_tokens,
+                            void *workspace, size_t workspace_bytes,
+                            PkvStream stream, char *error,
+                            size_t error_capacity);
+
+/* Paged decode that allocates nothing:pkv_paged_decode with its scratch in
  * a static 8 MiB device array inside this library instead of a workspace.
  * No counterpart in the SDK.  For callers that cannot allocate device memory
  * at call time (a serving loop whose device memory is planned once up front,

@@ -137,6 +137,9 @@ EXPORTS = {
     "pkv_decode_workspace_init": (_c_int, [_c_ptr, _c_size, _c_ptr, *_ERR]),
     "pkv_paged_decode": (_c_int, [_LP, _BP, _c_size, _c_ptr, ctypes.c_float, _c_ptr, _c_int,
                                   _c_size, _c_size, _c_ptr, _c_size, _c_ptr, *_ERR]),
+    "pkv_paged_decode_append": (_c_int, [_LP, _BP, _c_ptr, _c_ptr, _c_size, _c_ptr,
+                                         ctypes.c_float, _c_ptr, _c_int, _c_size, _c_size,
+                                         _c_ptr, _c_size, _c_ptr, *_ERR]),
     "pkv_paged_decode_static_scratch": (_c_int, [_LP, _BP, _c_size, _c_ptr, ctypes.c_float,
                                                  _c_ptr, _c_int, _c_size, _c_ptr, *_ERR]),
     "pkv_paged_prefill": (_c_int, [_LP, _BP, _c_size, _c_ptr, _c_ptr, _c_size, _c_size,
@@ -367,6 +370,20 @@ def paged_decode(layer: PkvPagedLayer, batch: PkvBatch, query, output, scale: fl
           max_seq_len, chunk_tokens, workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
 
 
+def paged_decode_append(layer: PkvPagedLayer, batch: PkvBatch, key_rows, value_rows, query,
+                        output, scale: float, max_seq_len: int, workspace, chunk_tokens: int = 0,
+                        stream=None) -> None:
+    """pkv_paged_decode_append: kv_append of one new row per sequence and
+    paged_decode in one call (one launch on the tensor-core path)."""
+    if key_rows.shape[0] != batch.batch or value_rows.shape[0] != batch.batch:
+        raise ValueError("one new K and V row per sequence")
+    q_heads = query.shape[-2]
+    _call("pkv_paged_decode_append", ctypes.byref(layer), ctypes.byref(batch),
+          key_rows.data_ptr(), value_rows.data_ptr(), q_heads, query.data_ptr(),
+          ctypes.c_float(scale), output.data_ptr(), _dtype_code(output), max_seq_len,
+          chunk_tokens, workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+
+
 def paged_decode_static_scratch(layer: PkvPagedLayer, batch: PkvBatch, query, output,
                                 scale: float, max_seq_len: int, stream=None) -> None:
     """pkv_paged_decode with the library's static device scratch (no workspace)."""
@@ -445,17 +462,19 @@ class PagedPool:
 
 class DecodeStepper:
     """One decode step of a fixed batch -- pkv_step_begin (one new token per
-    sequence), pkv_kv_append, pkv_paged_decode, pkv_step_end -- with every
-    argument converted once.  A step of a short batch runs for tens of
-    microseconds on the GPU; building the ctypes arguments, stream and dtype
-    lookups of the one-call wrappers again for each of the four calls would
-    make the Python host, not the GPU, set the step rate.  A failed call
-    rolls the open step back (pkv_step_end(0)) and raises."""
+    sequence), pkv_paged_decode_append (or, with fused=False, pkv_kv_append
+    then pkv_paged_decode), pkv_step_end -- with every argument converted
+    once.  A step of a short batch runs for tens of microseconds on the GPU;
+    building the ctypes arguments, stream and dtype lookups of the one-call
+    wrappers again for each call would make the Python host, not the GPU, set
+    the step rate.  A failed call rolls the open step back (pkv_step_end(0))
+    and raises."""
 
     def __init__(self, pool: PagedPool, layer: PkvPagedLayer, sequences: Sequence[int], query,
                  key_rows, value_rows, output, scale: float, max_seq_len: int, workspace,
-                 chunk_tokens: int = 0, stream=None):
+                 chunk_tokens: int = 0, stream=None, fused: bool = True):
         lib = load()
+        self.fused = fused
         n = len(sequences)
         self._lib = lib
         self._pool = pool.handle
@@ -496,13 +515,21 @@ class DecodeStepper:
                                   err, 512):
             self._fail("pkv_step_begin", False)
         lib.pkv_step_batch(self._pool, self._batch_ref)
-        if not lib.pkv_kv_append(self._layer_ref, self._batch_ref, None, self._k, self._v, self._n,
-                                 self._stream, err, 512):
-            self._fail("pkv_kv_append", True)
-        if not lib.pkv_paged_decode(self._layer_ref, self._batch_ref, self._q_heads, self._q,
-                                    self._scale, self._o, self._out_dtype, self._max_len,
-                                    self._chunk, self._ws, self._ws_bytes, self._stream, err, 512):
-            self._fail("pkv_paged_decode", True)
+        if self.fused:
+            if not lib.pkv_paged_decode_append(self._layer_ref, self._batch_ref, self._k, self._v,
+                                               self._q_heads, self._q, self._scale, self._o,
+                                               self._out_dtype, self._max_len, self._chunk,
+                                               self._ws, self._ws_bytes, self._stream, err, 512):
+                self._fail("pkv_paged_decode_append", True)
+        else:
+            if not lib.pkv_kv_append(self._layer_ref, self._batch_ref, None, self._k, self._v,
+                                     self._n, self._stream, err, 512):
+                self._fail("pkv_kv_append", True)
+            if not lib.pkv_paged_decode(self._layer_ref, self._batch_ref, self._q_heads, self._q,
+                                        self._scale, self._o, self._out_dtype, self._max_len,
+                                        self._chunk, self._ws, self._ws_bytes, self._stream, err,
+                                        512):
+                self._fail("pkv_paged_decode", True)
         if not lib.pkv_step_end(self._pool, 1, err, 512):
             self._fail("pkv_step_end", False)
 

@@ -521,6 +521,13 @@ struct TcArgs {
     // dynamic tail: smallest unit (tiles; bounds the pieces of one segment),
     // 0 = static units only
     int32_t min_unit;
+    // Fused append (pkv_paged_decode_append), else null: this step's new
+    // K/V row of every sequence ([batch][row_vecs] uint4), stored at
+    // position seq_lens[b] - 1 of the pools (same rows, as uint4) by the
+    // producer that loads the tile holding it, before that tile's TMA.
+    const uint4 *new_k, *new_v;
+    uint4 *kpool, *vpool;
+    int32_t row_vecs;  // uint4 per pool row (kv_heads * head_dim / 8)
 };
 
 // Tensor maps of one launch: K and V pools (one page x 64 columns per box)
@@ -858,6 +865,18 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         tma_prefetch_desc(&vmap);
         tma_prefetch_desc(&qmap);
     }
+    // The block-table rows of this launch into L2 while the kernel before
+    // this one finishes, so the producers' first table reads after the wait
+    // hit L2 rather than HBM.  A prefetch leaves no copy in registers or L1:
+    // an entry the previous kernel still writes is read later at its new
+    // value (L2 holds the one copy every SM sees).
+    {
+        const size_t bytes = (size_t)a.batch * (size_t)a.table_stride * 4u;
+        const char *tb = reinterpret_cast<const char *>(a.tables);
+        for (size_t off = ((size_t)blockIdx.x * kTcThreads + tid) * 128u; off < bytes;
+             off += (size_t)gridDim.x * kTcThreads * 128u)
+            prefetch_l2(tb + off);
+    }
     // Everything above touches only this CTA's shared memory and TMEM, so it
     // overlaps the previous kernel under programmatic dependent launch; from
     // here on global memory written by earlier kernels (pages, tables,
@@ -891,9 +910,13 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
 
     // One tile's pages of one pool (K: warp 0, V: warp 6) into stage slot
     // `dst` (two 64-column halves), completing on `bar`.  Lanes < np each load
-    // one page.
+    // one page.  `pool` non-null (fused append, only for the segment's last
+    // tile, whose last page holds position L - 1): lanes 0-15 first store
+    // the segment's 256 bytes of the new row, `nrow`, into that page; each
+    // fences its store against the async proxy and the warp converges before
+    // any lane issues the TMA, so the tile reads the new row.
     auto load_tile = [&](const CUtensorMap *map, uint64_t *bar, unsigned char *dst,
-                         const uint32_t *trow, int k, int L, int g) {
+                         const uint32_t *trow, int k, int L, int g, uint4 *pool, uint4 nrow) {
         const int ts = k * kTcTile;
         const int te = min(L, ts + kTcTile);
         const int p0 = ts / a.block_size;
@@ -909,6 +932,15 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             if (!good) record_fault(fault, kFaultPageOutOfRange);
         }
         const unsigned mask = __ballot_sync(0xffffffffu, good);
+        if (pool != nullptr) {
+            const uint32_t lp = __shfl_sync(0xffffffffu, pid, np - 1);
+            if (((mask >> (np - 1)) & 1u) != 0 && lane < 16) {
+                const int64_t prow = (int64_t)lp * a.block_size + (L - 1) % a.block_size;
+                pool[prow * a.row_vecs + g * 16 + lane] = nrow;
+                fence_proxy_async_global();
+            }
+            __syncwarp();
+        }
         if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)__popc(mask) * a.block_size * 256u);
         __syncwarp();
         if (good) {
@@ -940,6 +972,12 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             const Piece P = piece_at(t, ue, prefix, a);
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
+            // fused append: this piece ends its segment, so it loads the tile
+            // holding the new row; fetch the row now, store it at that tile
+            const bool app = a.new_k != nullptr && P.k1 == P.nt;
+            uint4 nrow = make_uint4(0, 0, 0, 0);
+            if (app && lane < 16)
+                nrow = __ldg(a.new_k + (int64_t)P.b * a.row_vecs + P.g * 16 + lane);
             if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) {
                 ok = false;
                 break;
@@ -967,7 +1005,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                     ok = false;
                     break;
                 }
-                load_tile(&kmap, &kfull[stage], sm + stage * kTcStageBytes, trow, k, L, P.g);
+                load_tile(&kmap, &kfull[stage], sm + stage * kTcStageBytes, trow, k, L, P.g,
+                          app && k == P.nt - 1 ? a.kpool : nullptr, nrow);
             }
             ++qi;
         }
@@ -1009,6 +1048,10 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             const Piece P = piece_at(t, ue, prefix, a);
             t += P.k1 - P.k0;
             const int L = __ldg(a.seq_lens + P.b);
+            const bool app = a.new_v != nullptr && P.k1 == P.nt;  // as the K producer
+            uint4 nrow = make_uint4(0, 0, 0, 0);
+            if (app && lane < 16)
+                nrow = __ldg(a.new_v + (int64_t)P.b * a.row_vecs + P.g * 16 + lane);
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const int stage = (int)(j % kTcStages);
@@ -1017,7 +1060,7 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                     break;
                 }
                 load_tile(&vmap, &vfull[stage], sm + stage * kTcStageBytes + 2 * kTcHalf, trow, k,
-                          L, P.g);
+                          L, P.g, app && k == P.nt - 1 ? a.vpool : nullptr, nrow);
             }
         }
         }
@@ -1271,6 +1314,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
         // empty sequences: no tile, zero output (the SDK's all-masked rule)
         for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
             if (__ldg(a.seq_lens + b) > 0) continue;
+            // a fused append needs room for its row (pkv_kv_append's rule)
+            if (a.new_k != nullptr && wt == 0) record_fault(fault, kFaultRowsMismatch);
             OT *ob = static_cast<OT *>(a.out) + (int64_t)b * q_heads * OD;
             if (row < OD)
                 for (int h = 0; h < q_heads; ++h) ob[h * OD + row] = from_f32<OT>(0.f);
@@ -1543,17 +1588,32 @@ int pkv_decode_workspace_init(void *workspace, size_t workspace_bytes, PkvStream
     return 1;
 }
 
-int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q_heads,
-                     const void *query, float scale, void *output, PkvDType output_dtype,
-                     size_t max_seq_len, size_t chunk_tokens, void *workspace,
-                     size_t workspace_bytes, PkvStream stream, char *error,
-                     size_t error_capacity) {
-    PKV_RANGE("pkv_paged_decode");
-    const char *what = "pkv_paged_decode";
+}  // extern "C"
+
+namespace pkv {
+namespace {
+
+// pkv_paged_decode, and with key_rows/value_rows non-null
+// pkv_paged_decode_append: the tensor-core kernel stores the new rows itself
+// (TcArgs::new_k), the CUDA-core path launches the append kernel first.
+int paged_decode_impl(const char *what, const PkvPagedLayer *layer, const PkvBatch *batch,
+                      const void *key_rows, const void *value_rows, size_t q_heads,
+                      const void *query, float scale, void *output, PkvDType output_dtype,
+                      size_t max_seq_len, size_t chunk_tokens, void *workspace,
+                      size_t workspace_bytes, PkvStream stream, char *error,
+                      size_t error_capacity) {
     if (layer == nullptr || batch == nullptr || query == nullptr || output == nullptr ||
         layer->key_pool == nullptr || layer->value_pool == nullptr ||
         batch->block_tables == nullptr || batch->seq_lens == nullptr) {
         pkv_internal_set_error(error, error_capacity, "%s: null argument", what);
+        return 0;
+    }
+    const bool fused = key_rows != nullptr || value_rows != nullptr;
+    if (fused && (key_rows == nullptr || value_rows == nullptr ||
+                  ((uintptr_t)key_rows | (uintptr_t)value_rows) % 16 != 0)) {
+        pkv_internal_set_error(error, error_capacity,
+                               "%s: key_rows and value_rows must both be given, 16-byte aligned",
+                               what);
         return 0;
     }
     if (layer->dtype != PKV_DTYPE_F16 && layer->dtype != PKV_DTYPE_BF16) {
@@ -1670,6 +1730,11 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         t.block_size = (int32_t)layer->block_size;
         t.block_count = (uint32_t)layer->block_count;
         t.scale_log2 = scale * pkv::kLog2e;
+        t.new_k = static_cast<const uint4 *>(key_rows);
+        t.new_v = static_cast<const uint4 *>(value_rows);
+        t.kpool = static_cast<uint4 *>(layer->key_pool);
+        t.vpool = static_cast<uint4 *>(layer->value_pool);
+        t.row_vecs = (int32_t)(kvh * hd / 8);
         // In-kernel merges need every segment to span at most
         // kInKernelMergeMax CTAs.  They also sit on the critical path of the
         // CTA that finishes last, so with few segments (each cut into many
@@ -1705,8 +1770,15 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
             sl.query = static_cast<const char *>(query) + b0 * q_heads * hd * 2;
             sl.q_row0 = (int32_t)(b0 * q_heads);
             sl.out = static_cast<char *>(output) + b0 * q_heads * hd * osz;
+            if (fused) {
+                sl.new_k += b0 * (size_t)t.row_vecs;
+                sl.new_v += b0 * (size_t)t.row_vecs;
+            }
             ok = pkv::dispatch_tc(sl, (int)group, pair, bf16, output_dtype, mp, ncta, s);
         }
+    } else if (fused && !pkv_kv_append(layer, batch, nullptr, key_rows, value_rows, batch->batch,
+                                       stream, error, error_capacity)) {
+        return 0;  // pkv_kv_append wrote the message
     } else if (layer->dtype == PKV_DTYPE_F16)
         ok = hd == 128 ? pkv::dispatch_group<128, __half>(a, (int)group, output_dtype, s)
                        : pkv::dispatch_group<64, __half>(a, (int)group, output_dtype, s);
@@ -1719,6 +1791,39 @@ int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q
         return 0;
     }
     return 1;
+}
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" {
+
+int pkv_paged_decode(const PkvPagedLayer *layer, const PkvBatch *batch, size_t q_heads,
+                     const void *query, float scale, void *output, PkvDType output_dtype,
+                     size_t max_seq_len, size_t chunk_tokens, void *workspace,
+                     size_t workspace_bytes, PkvStream stream, char *error,
+                     size_t error_capacity) {
+    PKV_RANGE("pkv_paged_decode");
+    return pkv::paged_decode_impl("pkv_paged_decode", layer, batch, nullptr, nullptr, q_heads,
+                                  query, scale, output, output_dtype, max_seq_len, chunk_tokens,
+                                  workspace, workspace_bytes, stream, error, error_capacity);
+}
+
+int pkv_paged_decode_append(const PkvPagedLayer *layer, const PkvBatch *batch,
+                            const void *key_rows, const void *value_rows, size_t q_heads,
+                            const void *query, float scale, void *output, PkvDType output_dtype,
+                            size_t max_seq_len, size_t chunk_tokens, void *workspace,
+                            size_t workspace_bytes, PkvStream stream, char *error,
+                            size_t error_capacity) {
+    PKV_RANGE("pkv_paged_decode_append");
+    const char *what = "pkv_paged_decode_append";
+    if (key_rows == nullptr || value_rows == nullptr) {
+        pkv_internal_set_error(error, error_capacity, "%s: null key_rows or value_rows", what);
+        return 0;
+    }
+    return pkv::paged_decode_impl(what, layer, batch, key_rows, value_rows, q_heads, query, scale,
+                                  output, output_dtype, max_seq_len, chunk_tokens, workspace,
+                                  workspace_bytes, stream, error, error_capacity);
 }
 
 int pkv_internal_take_decode_fault(uint32_t *code) {

@@ -85,6 +85,11 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// Brings the 128-byte line holding `p` into L2 (a hint: no register or L1
+// copy, so a later write to the line by any kernel is still seen).
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -93,6 +98,11 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
 // tensor cores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// Generic-proxy global-memory writes of this thread -> ordered before its
+// (or, after a warp or CTA barrier, another thread's) later TMA reads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");
 }
 
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {

@@ -233,13 +233,14 @@ def test_large_staging_spreads_over_ctas(lib, cuda):
     cache.free()
 
 
-def test_decode_stepper_back_to_back(lib, oracle_mod, cuda):
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_stepper_back_to_back(lib, oracle_mod, cuda, fused):
     """DecodeStepper steps queued back to back with no host synchronisation:
     the decode kernel releases its dependents early, so each step's staging
-    and append launch while the previous decode still streams.  Every step's
-    output (its own buffer) must match the oracle on the pages as they were
-    at that step, and the pages must end bit-exact.  A step whose decode
-    call is refused rolls back."""
+    (and, unfused, its append) launches while the previous decode still
+    streams.  Every step's output (its own buffer) must match the oracle on
+    the pages as they were at that step, and the pages must end bit-exact.
+    A step whose decode call is refused rolls back."""
     import torch
     n, kvh, qh, d, steps = 8, 2, 8, 128, 24
     cache = P.PagedKVCache(16, 1024, n)
@@ -274,7 +275,7 @@ def test_decode_stepper_back_to_back(lib, oracle_mod, cuda):
     ws = P.decode_workspace(n, qh, d, max_len, device=cuda)
     scale = float(1 / np.sqrt(d))
     stepper = P.DecodeStepper(pool, layer, seqs, dq[0], dk[0], dv[0], outs[0], scale, max_len,
-                              ws)
+                              ws, fused=fused)
     for i in range(steps):
         stepper.bind(dq[i], dk[i], dv[i], outs[i])
         stepper.step()
@@ -292,7 +293,8 @@ def test_decode_stepper_back_to_back(lib, oracle_mod, cuda):
     assert np.array_equal(k, mk) and np.array_equal(v, mv)
     # a refused decode (workspace too small) rolls the step back
     small = torch.zeros(64, dtype=torch.uint8, device=cuda)
-    bad = P.DecodeStepper(pool, layer, seqs, dq[0], dk[0], dv[0], outs[0], scale, max_len, small)
+    bad = P.DecodeStepper(pool, layer, seqs, dq[0], dk[0], dv[0], outs[0], scale, max_len, small,
+                          fused=fused)
     with pytest.raises(P.PkvError, match="workspace"):
         bad.step()
     assert [cache.length(s) for s in seqs] == lengths.tolist()
