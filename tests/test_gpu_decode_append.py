@@ -108,6 +108,15 @@ def test_fused_merge_kernel_path(lib, oracle_mod, cuda):
     _both_paths(case, oracle_mod, cuda, torch.float32, 50001, seed=87)
 
 
+def test_fused_batch_above_one_launch(lib, oracle_mod, cuda):
+    """More sequences than one tensor-core launch holds (1024): each sliced
+    launch reads the new rows of its own sequences."""
+    import torch
+    lengths = (W.uniform(5, 1100) * 300).astype(np.int64) + 1
+    case = PagedCase(lengths, 4, 1, 128, 16, "f16", seed=91, device=cuda)
+    _both_paths(case, oracle_mod, cuda, torch.float32, int(lengths.max()), seed=92)
+
+
 def test_fused_empty_sequence_records_fault(lib, oracle_mod, cuda):
     """A sequence of length 0 has no position for its row: nothing is
     stored, its output is zero and fault code 3 is recorded (pkv_kv_append's
