@@ -106,6 +106,28 @@ def test_kernel_entry_points_reject_bad_arguments(lib):
                                 ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256, 8, None, e,
                                 len(e)) == 0
     assert b"workspace" in e.value
+    # decode with the append: the rows are checked first, then everything
+    # pkv_paged_decode checks, before any device work
+    e = _err()
+    assert lib.pkv_paged_decode_append(ctypes.byref(layer), ctypes.byref(batch), None, 16, 4, 16,
+                                       ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256,
+                                       1 << 20, None, e, len(e)) == 0
+    assert b"null key_rows" in e.value
+    e = _err()
+    assert lib.pkv_paged_decode_append(ctypes.byref(layer), ctypes.byref(batch), 16, 24, 4, 16,
+                                       ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256,
+                                       1 << 20, None, e, len(e)) == 0
+    assert b"16-byte aligned" in e.value
+    e = _err()
+    assert lib.pkv_paged_decode_append(ctypes.byref(layer), ctypes.byref(batch), 16, 16, 6, 16,
+                                       ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256,
+                                       1 << 20, None, e, len(e)) == 0
+    assert b"q_heads/kv_heads" in e.value and b"pkv_paged_decode_append" in e.value
+    e = _err()
+    assert lib.pkv_paged_decode_append(ctypes.byref(layer), ctypes.byref(batch), 16, 16, 4, 16,
+                                       ctypes.c_float(0.1), 16, P.PKV_DTYPE_F32, 64, 0, 256, 8,
+                                       None, e, len(e)) == 0
+    assert b"workspace" in e.value
     e = _err()
     assert lib.pkv_step_begin(None, None, None, None, 0, None, e, len(e)) == 0
     assert lib.pkv_step_end(None, 1, e, len(e)) == 0
