@@ -908,25 +908,43 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
     if (blockIdx.x == 0 && a.tile_prefix != nullptr)
         for (int b = tid; b <= a.batch; b += kTcThreads) a.tile_prefix[b] = prefix[b];
 
+    // Block-table entries of a piece, 32 pages at a time, one per lane of a
+    // producer warp: one load round trip serves the pages of several tiles
+    // (four at 16-token pages), and a piece's first window is requested when
+    // the piece starts, before its producer waits for a free stage slot.
+    // Entries past the table row read as an invalid page id.
+    struct TableWindow {
+        int first;       // page index held by lane 0
+        uint32_t entry;  // page first + lane
+    };
+    auto window_at = [&](const uint32_t *trow, int first) {
+        TableWindow w;
+        w.first = first;
+        w.entry = first + lane < a.table_stride ? __ldg(trow + first + lane) : 0xffffffffu;
+        return w;
+    };
     // One tile's pages of one pool (K: warp 0, V: warp 6) into stage slot
     // `dst` (two 64-column halves), completing on `bar`.  Lanes < np each load
-    // one page.  `pool` non-null (fused append, only for the segment's last
-    // tile, whose last page holds position L - 1): lanes 0-15 first store
-    // the segment's 256 bytes of the new row, `nrow`, into that page; each
-    // fences its store against the async proxy and the warp converges before
-    // any lane issues the TMA, so the tile reads the new row.
+    // one page, its id taken from the window `win` (reloaded when the tile's
+    // pages leave it).  `pool` non-null (fused append, only for the segment's
+    // last tile, whose last page holds position L - 1): lanes 0-15 first
+    // store the segment's 256 bytes of the new row, `nrow`, into that page;
+    // each fences its store against the async proxy and the warp converges
+    // before any lane issues the TMA, so the tile reads the new row.
     auto load_tile = [&](const CUtensorMap *map, uint64_t *bar, unsigned char *dst,
-                         const uint32_t *trow, int k, int L, int g, uint4 *pool, uint4 nrow) {
+                         const uint32_t *trow, TableWindow &win, int k, int L, int g,
+                         uint4 *pool, uint4 nrow) {
         const int ts = k * kTcTile;
         const int te = min(L, ts + kTcTile);
         const int p0 = ts / a.block_size;
-        const int np = (te - ts + a.block_size - 1) / a.block_size;
+        const int np = (te - ts + a.block_size - 1) / a.block_size;  // 1..8
+        if (p0 < win.first || p0 + np > win.first + 32) win = window_at(trow, p0);
+        const uint32_t e = __shfl_sync(0xffffffffu, win.entry, (p0 - win.first + lane) & 31);
         uint32_t pid = 0;
         bool good = false;
         if (lane < np) {
-            const int pi = p0 + lane;
-            if (pi < a.table_stride) {
-                pid = __ldg(trow + pi);
+            if (p0 + lane < a.table_stride) {
+                pid = e;
                 good = pid < a.block_count;
             }
             if (!good) record_fault(fault, kFaultPageOutOfRange);
@@ -978,6 +996,8 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             uint4 nrow = make_uint4(0, 0, 0, 0);
             if (app && lane < 16)
                 nrow = __ldg(a.new_k + (int64_t)P.b * a.row_vecs + P.g * 16 + lane);
+            const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
+            TableWindow win = window_at(trow, P.k0 * kTcTile / a.block_size);
             if (!mbar_wait(&q_empty[qi & 1], ((qi >> 1) & 1) ^ 1, abort_flag, fault)) {
                 ok = false;
                 break;
@@ -998,14 +1018,13 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
                 }
             }
             __syncwarp();
-            const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const int stage = (int)(j % kTcStages);
                 if (!mbar_wait(&kempty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
                     ok = false;
                     break;
                 }
-                load_tile(&kmap, &kfull[stage], sm + stage * kTcStageBytes, trow, k, L, P.g,
+                load_tile(&kmap, &kfull[stage], sm + stage * kTcStageBytes, trow, win, k, L, P.g,
                           app && k == P.nt - 1 ? a.kpool : nullptr, nrow);
             }
             ++qi;
@@ -1053,14 +1072,15 @@ paged_decode_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap kmap,
             if (app && lane < 16)
                 nrow = __ldg(a.new_v + (int64_t)P.b * a.row_vecs + P.g * 16 + lane);
             const uint32_t *trow = a.tables + (int64_t)P.b * a.table_stride;
+            TableWindow win = window_at(trow, P.k0 * kTcTile / a.block_size);
             for (int k = P.k0; k < P.k1; ++k, ++j) {
                 const int stage = (int)(j % kTcStages);
                 if (!mbar_wait(&vempty[stage], ((j / kTcStages) & 1) ^ 1, abort_flag, fault)) {
                     ok = false;
                     break;
                 }
-                load_tile(&vmap, &vfull[stage], sm + stage * kTcStageBytes + 2 * kTcHalf, trow, k,
-                          L, P.g, app && k == P.nt - 1 ? a.vpool : nullptr, nrow);
+                load_tile(&vmap, &vfull[stage], sm + stage * kTcStageBytes + 2 * kTcHalf, trow,
+                          win, k, L, P.g, app && k == P.nt - 1 ? a.vpool : nullptr, nrow);
             }
         }
         }
