@@ -107,7 +107,8 @@ kv_rows_kernel(uint4 *__restrict__ kpool, uint4 *__restrict__ vpool,
 // entries) spreads over several, which count themselves out on `arrive`
 // (a device word, zero between launches).  The last CTA to finish writes
 // `ticket` to the slot's host word, which tells the host the slot may be
-// refilled.
+// refilled; a one-CTA staging whose reads all precede its grid-dependency
+// wait writes it before that wait.
 __global__ void __launch_bounds__(512)
 stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ dev_lens,
                    int batch, int max_batch, const PkvTablePatch *__restrict__ host_patches,
@@ -125,6 +126,17 @@ stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ 
     if (first < batch) len0 = host_lens[first];
     if (first <= batch) off0 = host_lens[max_batch + first];
     if (first < count) p0 = host_patches[first];
+    // A launch whose every slot read is one of those first items (one CTA,
+    // batch + 1 lengths and count patches within its threads: every decode
+    // step) hands the slot back before the wait.  Its reads have returned
+    // once the CTA passes the barrier, and the ticket orders nothing else:
+    // the host only refills the slot after seeing it.  The kernel after this
+    // one then waits for nothing but the device writes below.
+    const bool prefetched = gridDim.x == 1 && batch < (int)blockDim.x && count <= blockDim.x;
+    if (prefetched) {
+        __syncthreads();
+        if (threadIdx.x == 0) *host_done = ticket;
+    }
     pdl_wait();  // the previous step's kernels no longer read the table or this slot
     for (int64_t i = first; i <= batch; i += step) {
         if (i < batch) dev_lens[i] = i == first ? len0 : host_lens[i];
@@ -138,6 +150,7 @@ stage_apply_kernel(const int32_t *__restrict__ host_lens, int32_t *__restrict__ 
         }
         table[(int64_t)p.row * stride + p.index] = p.page;
     }
+    if (prefetched) return;
     __syncthreads();  // every read of the host slot by this CTA has returned
     if (threadIdx.x == 0) {
         __threadfence();
