@@ -294,7 +294,9 @@ int pkv_internal_stage_apply(const int32_t *host_lens, int32_t *dev_lens, size_t
                              uint32_t *table, size_t table_stride, size_t table_rows,
                              uint32_t *arrive, uint32_t *host_done, uint32_t ticket,
                              PkvStream stream) {
-    const unsigned threads = count > 256 || batch > 256 ? 512u : 256u;
+    // batch + 1 lengths and the patches within one CTA's threads let the
+    // kernel read the whole slot before its grid-dependency wait
+    const unsigned threads = count > 256 || batch >= 256 ? 512u : 256u;
     const size_t work = count > batch ? count : batch;
     const size_t per_cta = 4096;  // bus reads in flight per CTA, roughly
     const unsigned grid = (unsigned)(work <= per_cta ? 1 : (work + per_cta - 1) / per_cta < 64
